@@ -1,0 +1,164 @@
+/*
+ * prismkv_b200.h -- C ABI of the B200 (sm_100a) PrismKV quantized-KV hot path.
+ *
+ * Every entry point takes plain device pointers, element counts, strides and
+ * a CUDA stream (passed as `void *`, it is a `cudaStream_t`), returns an int
+ * status (0 = PKV_OK) and never allocates device memory.  Buffers are owned
+ * by the caller.  Kernels are enqueued on the given stream; no entry point
+ * synchronises the host.  Entry points are re-entrant: concurrent calls on
+ * different streams are safe as long as they do not share a workspace.
+ *
+ * Units: dim = head dimension d (a multiple of 3), m = dim / 3 triplets,
+ * codes are packed (i_z << (bits_r + bits_theta)) | i_flat.
+ *
+ * Reference interfaces replaced (PrismKV v1.4.1, paths inside that project):
+ *   pkv_encode         StackedPlaneQuantizer.encode   src/prismkv/quantizer/stacked_plane.py:210-262
+ *                      (+ LearnedSliceCodebook.encode_xy learned_codebook.py:217-248,
+ *                         LloydMaxQuantizer1D.encode lloyd_max.py:106-124)
+ *   pkv_decode         StackedPlaneQuantizer.decode   src/prismkv/quantizer/stacked_plane.py:268-327
+ *                      (+ decode_xy learned_codebook.py:250-269, BiasTable.apply
+ *                         bias_correction.py:58-91, LloydMaxQuantizer1D.decode lloyd_max.py:126-140)
+ *   pkv_attn_decode    PolarAttentionApprox.forward   src/prismkv/quantizer/polar_attention.py:277-309
+ *                      fused with decode of V; no reference kernel exists
+ *   pkv_polar_scores   prismkv_cuda.polar_attn_fwd    src/prismkv/cuda/prismkv_cuda.cpp:9-18,
+ *                      kernel src/prismkv/cuda/polar_attn_kernel.cu:142-336,
+ *                      Python contract src/prismkv/cuda/__init__.py:23-61
+ *   pkv_lse_combine    (new) log-sum-exp merge of split-sequence partials
+ */
+#ifndef PRISMKV_B200_H
+#define PRISMKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PKV_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define PKV_API __attribute__((visibility("default")))
+#else
+#define PKV_API
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+    PKV_OK = 0,
+    PKV_ERR_INVALID = 1,      /* null pointer, bad shape, bits out of range      */
+    PKV_ERR_UNSUPPORTED = 2,  /* well-formed but outside what this build runs    */
+    PKV_ERR_ALIGNMENT = 3,    /* pointer or stride misaligned for the call       */
+    PKV_ERR_WORKSPACE = 4,    /* workspace missing or smaller than required      */
+    PKV_ERR_CUDA = 5,         /* CUDA runtime reported an error (launch/config)  */
+    PKV_ERR_DEVICE = 6        /* a kernel flagged an error (bounded wait expired)*/
+};
+
+/* ---- element types ----------------------------------------------------- */
+enum { PKV_F32 = 0, PKV_BF16 = 1, PKV_F16 = 2 };
+
+/* ---- quantizer state ---------------------------------------------------- *
+ * All table pointers are device pointers.  Tables are built on the host
+ * once per quantizer (they are the quantizer's parameters, not data):
+ *   z_thr    (2^bits_z - 1)   i_z  = #{b : z >= z_thr[b]}            (ascending)
+ *   r2_thr   (2^bits_r - 1)   i_r  = #{b : x*x + y*y >= r2_thr[b]}   (polar path)
+ *   th_thr   (2^bits_theta-1) i_th = #{b : atan2(y, x) >= th_thr[b]} (polar path)
+ *   codebook (2^bits_z, K, 2) learned (x, y) centroids, K = 2^(bits_r+bits_theta)
+ *   dec_z    (2^bits_z)       dequantized z per bin, BiasTable folded in
+ *   dec_xy   (xy_per_z ? 2^bits_z * K : K, 2) dequantized (x, y), bias folded in
+ * z_hi: z >= z_hi maps to bin 0 (uniform bins: the reference's int64
+ * conversion of an out-of-range floor); NaN when unused.  z_nan_bin: bin of
+ * a NaN z (0 for uniform bins, 2^bits_z - 1 for Lloyd-Max boundaries).     */
+typedef struct pkv_codec {
+    int32_t dim;
+    int32_t bits_z, bits_r, bits_theta;   /* each 1..8, sum <= 16            */
+    int32_t xy_mode;                      /* 0 uniform polar, 1 codebook     */
+    int32_t xy_per_z;                     /* dec_xy indexed by full code     */
+    int32_t z_nan_bin;
+    float z_hi;
+    const float *R;                       /* (dim, dim) row-major rotation   */
+    const float *z_thr;
+    const float *r2_thr;
+    const float *th_thr;
+    const float *codebook;
+    const float *dec_z;
+    const float *dec_xy;
+} pkv_codec;
+
+/* ---- decode attention -------------------------------------------------- *
+ * out[b, h, :] = softmax(q'[b,h] . Khat^T * scale) . Vhat  @ R
+ * with q' = q @ R^T, Khat/Vhat the rotated-space dequantized codes, and
+ * KV head h / (q_heads / kv_heads) serving query head h (grouped heads).
+ * Codes live at k_codes + b*kv_batch_stride + hk*kv_head_stride + t*m (in
+ * code units), t < seq_lens[b] (or seq_len when seq_lens is NULL).
+ * partial_only != 0: write, per (b, h), the unnormalised rotated-space
+ * partial [m_max, l, o[0..dim-1]] (natural-log max of score*scale,
+ * l = sum exp(s - m_max), o = sum exp(s - m_max) * Vhat) to
+ * partial_out + (b*q_heads + h) * (dim + 2), instead of out.                */
+typedef struct pkv_attn_args {
+    int32_t batch, q_heads, kv_heads, seq_len;
+    const void *q;                 /* (batch, q_heads, dim) of q_dtype          */
+    int32_t q_dtype;
+    int64_t q_batch_stride, q_head_stride;       /* elements                    */
+    const void *k_codes, *v_codes;
+    int32_t code_bytes;                          /* 1 (uint8) or 2 (u/int16)     */
+    int64_t kv_batch_stride, kv_head_stride;     /* codes                       */
+    const int32_t *seq_lens;                     /* device, optional            */
+    float scale;
+    float *out;                                  /* (batch, q_heads, dim) f32   */
+    int64_t out_batch_stride, out_head_stride;   /* elements                    */
+    int32_t num_splits;                          /* 0 = choose                  */
+    int32_t partial_only;
+    float *partial_out;
+} pkv_attn_args;
+
+/* ---- entry points ------------------------------------------------------ */
+PKV_API int pkv_abi_version(void);
+PKV_API const char *pkv_strerror(int status);
+
+/* Reads (and optionally clears) the device error word set by a kernel whose
+ * bounded wait expired.  Synchronous on the current device.                */
+PKV_API int pkv_device_error(int32_t *flag_out, int32_t clear);
+
+/* codes[n, j] for n < N, j < m.  x: (N, dim) rows of x_dtype, row stride
+ * x_stride elements.  codes: row stride code_stride codes of code_bytes
+ * (1 = uint8, 2 = uint16, 8 = int64).                                     */
+PKV_API int pkv_encode(const pkv_codec *c, const void *x, int32_t x_dtype, int64_t n,
+               int64_t x_stride, void *codes, int32_t code_bytes,
+               int64_t code_stride, void *stream);
+
+/* out[n, :] = dequant(codes[n, :]) @ R, out of out_dtype, row stride
+ * out_stride elements.                                                    */
+PKV_API int pkv_decode(const pkv_codec *c, const void *codes, int32_t code_bytes,
+               int64_t n, int64_t code_stride, void *out, int32_t out_dtype,
+               int64_t out_stride, void *stream);
+
+/* Bytes of workspace pkv_attn_decode needs for these arguments (0 when one
+ * split per KV head suffices).  The workspace must be zeroed once
+ * (pkv_workspace_init) before its first use; every call leaves it zeroed. */
+PKV_API size_t pkv_attn_workspace_size(const pkv_codec *c, const pkv_attn_args *a);
+PKV_API int pkv_workspace_init(void *workspace, size_t bytes, void *stream);
+PKV_API int pkv_attn_decode(const pkv_codec *c, const pkv_attn_args *a,
+                    void *workspace, size_t workspace_bytes, void *stream);
+
+/* Merge n_parts partials per row (row r of part p at
+ * partials + p*part_stride + r*(dim+2)), normalise, rotate back with R and
+ * write out + r*out_row_stride (dim floats).                              */
+PKV_API int pkv_lse_combine(const pkv_codec *c, const float *partials, int32_t n_parts,
+                    int64_t part_stride, int32_t rows, float *out,
+                    int64_t out_row_stride, void *stream);
+
+/* Scores of prismkv_cuda.polar_attn_fwd: out[b,h,i,j] =
+ * scale * <q_rot[b,h,i], dequant(k_codes[b,h,j])> with the uniform polar
+ * dequant.  q_params (host): {z_min, delta_z, r_max, delta_r, delta_theta,
+ * scale}; bits (host): {bits_z, bits_r, bits_theta}.  q_rot, out fp32
+ * contiguous; k_codes contiguous (B, H, Sk, dim/3).                       */
+PKV_API int pkv_polar_scores(const float *q_rot, const void *k_codes, int32_t code_bytes,
+                     int32_t B, int32_t H, int32_t Sq, int32_t Sk, int32_t dim,
+                     const float *q_params, const int32_t *bits, float *out,
+                     void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PRISMKV_B200_H */

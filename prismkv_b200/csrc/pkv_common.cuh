@@ -1,0 +1,139 @@
+// pkv_common.cuh -- shared device helpers for the PrismKV sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/prismkv_b200.h"
+
+#define PKV_MAX_BITS 8          // per component
+#define PKV_MAX_TOTAL_BITS 16   // per code
+#define PKV_NUM_SMS_B200 148
+
+namespace pkv {
+
+// Device error word: set when a bounded wait expires; read by pkv_device_error.
+__device__ int32_t g_device_error = 0;   // single definition: the library is one translation unit
+
+enum : int32_t { kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3 };
+
+__device__ __forceinline__ void flag_error(int32_t code) { atomicCAS(&g_device_error, 0, code); }
+
+// ---------------------------------------------------------------------------
+// element loads
+// ---------------------------------------------------------------------------
+template <int DT> struct Elem;
+template <> struct Elem<PKV_F32> {
+    using T = float;
+    static __device__ __forceinline__ float load(const T* p) { return __ldg(p); }
+    static __device__ __forceinline__ void store(T* p, float v) { *p = v; }
+};
+template <> struct Elem<PKV_BF16> {
+    using T = __nv_bfloat16;
+    static __device__ __forceinline__ float load(const T* p) { return __bfloat162float(__ldg(p)); }
+    static __device__ __forceinline__ void store(T* p, float v) { *p = __float2bfloat16_rn(v); }
+};
+template <> struct Elem<PKV_F16> {
+    using T = __half;
+    static __device__ __forceinline__ float load(const T* p) { return __half2float(__ldg(p)); }
+    static __device__ __forceinline__ void store(T* p, float v) { *p = __float2half_rn(v); }
+};
+
+template <int CB> struct Code;
+template <> struct Code<1> {
+    using T = uint8_t;
+    static __device__ __forceinline__ uint32_t load(const T* p) { return __ldg(p); }
+    static __device__ __forceinline__ void store(T* p, uint32_t v) { *p = (T)v; }
+};
+template <> struct Code<2> {
+    using T = uint16_t;
+    static __device__ __forceinline__ uint32_t load(const T* p) { return __ldg(p); }
+    static __device__ __forceinline__ void store(T* p, uint32_t v) { *p = (T)v; }
+};
+template <> struct Code<8> {
+    using T = int64_t;
+    static __device__ __forceinline__ uint32_t load(const T* p) { return (uint32_t)__ldg(p); }
+    static __device__ __forceinline__ void store(T* p, uint32_t v) { *p = (T)v; }
+};
+
+// Count of ascending thresholds t[0..n-1] with v >= t[i]  (branch-free
+// binary search; n = 2^bits - 1, so the search runs `bits` steps).  NaN
+// compares false everywhere and yields 0.
+__device__ __forceinline__ int count_ge(const float* t, int bits, float v) {
+    int lo = 0;  // answer in [lo, lo + 2^k)
+    #pragma unroll 1
+    for (int k = bits - 1; k >= 0; --k) {
+        int probe = lo + (1 << k);         // candidate count; threshold index probe-1
+        lo = (v >= t[probe - 1]) ? probe : lo;
+    }
+    return lo;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier / bulk-copy PTX (sm_90+), with bounded waits
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete; gives up after ~`limit`
+// polls (each try_wait itself blocks for a hardware-defined interval), sets
+// the device error word and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t err,
+                                          uint32_t limit = (1u << 22)) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (i > 64) __nanosleep(64);
+    }
+    flag_error(err);
+    return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+}  // namespace pkv

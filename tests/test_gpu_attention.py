@@ -1,0 +1,194 @@
+"""GPU parity of the fused dequant + flash-decoding kernel (pkv_attn_decode).
+
+Outputs are compared with the oracle's fp64 attention over the same codes
+(and with the reference's own outputs in the golden fixtures).  Tolerance:
+max abs error <= 1e-3 for every query dtype (the north_star allows 2e-2 for
+bf16 queries; the kernel computes in fp32 on the exactly upcast query).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import load_golden, params_from, quantizer_from
+from prismkv_b200 import BiasTable, LearnedSliceCodebook, StackedPlaneQuantizer, decode_attention
+from prismkv_b200.synthetic import synthetic_bias, synthetic_codebook
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 1e-3
+
+
+def test_attention_matches_reference_polar_attention(cuda_ready):
+    f = load_golden("attn_v1")
+    q = quantizer_from(f)
+    qt = torch.from_numpy(f["q"]).to(DEV)
+    out = decode_attention(q, qt, torch.from_numpy(f["k_codes"]).to(DEV), torch.from_numpy(f["v_codes"]).to(DEV))
+    np.testing.assert_allclose(out.cpu().numpy(), f["out"][:, :, 0], atol=TOL)
+
+
+def test_attention_matches_reference_learned_gqa(cuda_ready):
+    f = load_golden("attn_v2_gqa")
+    q = quantizer_from(f)
+    out = decode_attention(q, torch.from_numpy(f["q"]).to(DEV), torch.from_numpy(f["k_codes"]).to(DEV),
+                           torch.from_numpy(f["v_codes"]).to(DEV))
+    np.testing.assert_allclose(out.cpu().numpy(), f["out"][:, :, 0], atol=TOL)
+
+
+def _setup(variant, bits, dim=96, seed=0):
+    q = StackedPlaneQuantizer(dim, *bits, seed=42)
+    Cz, K = 1 << bits[0], 1 << (bits[1] + bits[2])
+    if "learned" in variant:
+        q._codebooks = LearnedSliceCodebook(synthetic_codebook(Cz, K, q.r_max, 11), Cz, K, q.z_min, q.z_max, q.r_max)
+    if "bias" in variant:
+        q._bias = BiasTable(synthetic_bias(Cz, 12), delta_z=(q.z_max - q.z_min) / Cz)
+    if "lloyd" in variant:
+        q.calibrate_lloyd_max_z(torch.randn(2048, dim, generator=torch.Generator().manual_seed(5)).to(DEV))
+    p = oracle.QuantParams(dim=dim, bits_z=bits[0], bits_r=bits[1], bits_theta=bits[2],
+                           z_min=q.z_min, z_max=q.z_max, r_max=q.r_max)
+    if q._codebooks is not None:
+        p.codebook = q._codebooks.codebooks.numpy()
+    if q._lloyd_max_z is not None:
+        p.lloyd_boundaries = q._lloyd_max_z.boundaries.numpy()
+        p.lloyd_centroids = q._lloyd_max_z.centroids.numpy()
+    if q._bias is not None:
+        p.bias_table = q._bias.table.numpy()
+        p.bias_delta_z = q._bias.delta_z
+    return q, p
+
+
+def _codes(q, B, H, S, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    k = torch.randn(B * H * S, q.dim, generator=g, device=DEV)
+    v = torch.randn(B * H * S, q.dim, generator=g, device=DEV) * 1.5
+    kc = q.encode_compact(k).view(B, H, S, q.m)
+    vc = q.encode_compact(v).view(B, H, S, q.m)
+    return kc, vc
+
+
+CASES = [
+    # B, Hq, Hkv, S, variant, bits, qdtype, splits
+    (1, 8, 8, 1024, "v1", (4, 4, 4), torch.float32, 0),          # cpu-roundtrip shape
+    (2, 8, 8, 1, "v1", (4, 4, 4), torch.float32, 0),
+    (2, 8, 8, 3, "v1", (4, 4, 4), torch.float32, 0),
+    (2, 8, 8, 63, "v1", (4, 4, 4), torch.bfloat16, 0),
+    (2, 8, 8, 65, "v1", (4, 4, 4), torch.float16, 0),
+    (2, 8, 8, 257, "v1", (4, 4, 4), torch.float32, 0),
+    (2, 32, 8, 1000, "learned_bias", (4, 4, 4), torch.bfloat16, 0),  # learned-gqa shape, short
+    (1, 4, 4, 700, "lloyd", (4, 4, 4), torch.float32, 0),
+    (1, 8, 4, 900, "lloyd_learned_bias", (4, 4, 4), torch.float32, 0),
+    (2, 4, 4, 513, "v1", (3, 3, 2), torch.float32, 0),            # uint8 codes
+    (2, 4, 4, 513, "learned", (3, 3, 2), torch.float32, 0),
+    (1, 4, 2, 300, "v1", (4, 4, 4), torch.float32, 0),            # group 2
+    (1, 16, 2, 300, "v1", (4, 4, 4), torch.float32, 0),           # group 8
+    (1, 6, 2, 100, "v1", (4, 4, 4), torch.float32, 0),            # group 3 (padded to 4)
+    (2, 8, 4, 2000, "v1", (4, 4, 4), torch.float32, 1),
+    (2, 8, 4, 2000, "v1", (4, 4, 4), torch.float32, 2),
+    (2, 8, 4, 2000, "v1", (4, 4, 4), torch.float32, 7),
+    (2, 8, 4, 2000, "v1", (4, 4, 4), torch.float32, 16),
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,variant,bits,qdt,splits", CASES)
+def test_attention_matches_oracle(cuda_ready, B, Hq, Hkv, S, variant, bits, qdt, splits):
+    q, p = _setup(variant, bits)
+    kc, vc = _codes(q, B, Hkv, S, seed=S + Hq)
+    qv = torch.randn(B, Hq, 96, generator=torch.Generator(device=DEV).manual_seed(7), device=DEV).to(qdt)
+    out = decode_attention(q, qv, kc, vc, num_splits=splits)
+    ref = oracle.attention(qv.float().cpu().numpy(), kc.cpu().numpy().astype(np.int64),
+                           vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+
+
+@pytest.mark.parametrize("dim", [66, 192, 129])
+def test_attention_other_head_dims(cuda_ready, dim):
+    """d=66 (GPT-2 64 padded; 44-byte rows -> plain-load path), d=192 (two triplets per lane)."""
+    q, p = _setup("v1", (4, 4, 4), dim=dim)
+    kc, vc = _codes(q, 1, 4, 300, seed=dim)
+    qv = torch.randn(1, 4, dim, generator=torch.Generator(device=DEV).manual_seed(1), device=DEV)
+    out = decode_attention(q, qv, kc, vc)
+    ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64), vc.cpu().numpy().astype(np.int64),
+                           q.R.numpy(), p)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+
+
+def test_attention_ragged_and_empty_rows(cuda_ready):
+    q, p = _setup("v1", (4, 4, 4))
+    kc, vc = _codes(q, 3, 8, 512, seed=2)
+    qv = torch.randn(3, 8, 96, generator=torch.Generator(device=DEV).manual_seed(2), device=DEV)
+    lens = torch.tensor([512, 0, 77], dtype=torch.int32, device=DEV)
+    for splits in (0, 1, 3):
+        out = decode_attention(q, qv, kc, vc, seq_lens=lens, num_splits=splits)
+        ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64), vc.cpu().numpy().astype(np.int64),
+                               q.R.numpy(), p, seq_lens=lens.cpu().numpy())
+        np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+        assert (out[1] == 0).all()
+
+
+def test_attention_capacity_strided_cache(cuda_ready):
+    """Codes inside a larger preallocated cache (head stride = capacity * m)."""
+    q, p = _setup("v1", (4, 4, 4))
+    cap, S = 1000, 640
+    kfull, vfull = _codes(q, 2, 4, cap, seed=3)
+    kc, vc = kfull[:, :, :S], vfull[:, :, :S]
+    qv = torch.randn(2, 4, 96, generator=torch.Generator(device=DEV).manual_seed(3), device=DEV)
+    out = decode_attention(q, qv, kc, vc)
+    ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64), vc.cpu().numpy().astype(np.int64),
+                           q.R.numpy(), p)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+
+
+def test_attention_partials_and_lse_combine(cuda_ready):
+    """Shard the sequence (uneven, one empty shard), keep partials, merge: equals unsplit."""
+    q, p = _setup("v1", (4, 4, 4))
+    B, H, S = 2, 8, 1500
+    kc, vc = _codes(q, B, H, S, seed=4)
+    qv = torch.randn(B, H, 96, generator=torch.Generator(device=DEV).manual_seed(4), device=DEV)
+    codec = q.codec(torch.device(DEV))
+    bounds = [0, 700, 700, 1500]
+    parts = []
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        parts.append(codec.attention(qv, kc[:, :, a:b], vc[:, :, a:b], partial=True).view(B * H, 98))
+    merged = codec.combine(torch.stack(parts)).view(B, H, 96)
+    ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64), vc.cpu().numpy().astype(np.int64),
+                           q.R.numpy(), p)
+    np.testing.assert_allclose(merged.cpu().numpy(), ref, atol=TOL, rtol=0)
+    # partial contents against an fp64 restatement (natural-log max, l, o in rotated space)
+    pa = parts[0].view(B, H, 98).cpu().numpy().astype(np.float64)
+    kr = oracle.dequant_rotated(kc[:, :, :700].cpu().numpy().reshape(-1, 32), p).reshape(B, H, 700, 96)
+    vr = oracle.dequant_rotated(vc[:, :, :700].cpu().numpy().reshape(-1, 32), p).reshape(B, H, 700, 96)
+    qr = qv.cpu().numpy().astype(np.float64) @ q.R.numpy().astype(np.float64).T
+    s = np.einsum("bhd,bhsd->bhs", qr, kr) * 96 ** -0.5
+    mx = s.max(-1)
+    w = np.exp(s - mx[..., None])
+    np.testing.assert_allclose(pa[..., 0], mx, atol=1e-4)
+    np.testing.assert_allclose(pa[..., 1], w.sum(-1), rtol=1e-4)
+    np.testing.assert_allclose(pa[..., 2:], np.einsum("bhs,bhsd->bhd", w, vr), rtol=1e-4, atol=1e-3)
+    empty = parts[1].view(B, H, 98)
+    assert torch.isinf(empty[..., 0]).all() and (empty[..., 1:] == 0).all()
+
+
+def test_attention_repeated_calls_reuse_workspace(cuda_ready):
+    q, _ = _setup("v1", (4, 4, 4))
+    kc, vc = _codes(q, 2, 8, 3000, seed=5)
+    qv = torch.randn(2, 8, 96, generator=torch.Generator(device=DEV).manual_seed(5), device=DEV)
+    outs = [decode_attention(q, qv, kc, vc, num_splits=6).clone() for _ in range(4)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    from prismkv_b200 import _lib
+    assert _lib.device_error() == 0
+
+
+def test_phi3_decode_full_size(cuda_ready):
+    """The benchmark workload at full size (B=8, 32 heads, S=4096) against the oracle."""
+    from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
+    w = WORKLOADS["phi3-decode"]
+    q = make_quantizer(w)
+    kc, vc = make_kv_codes(w, q, DEV)
+    qv = make_query(w, DEV)
+    out = decode_attention(q, qv, kc, vc)
+    p = oracle.QuantParams.default(96)
+    ref = oracle.attention(qv.float().cpu().numpy(), kc.cpu().numpy().astype(np.int64),
+                           vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)

@@ -1,0 +1,116 @@
+"""Host tables (thresholds, LUTs) reproduce the reference's fp32 binning exactly.
+
+The kernels compute i = #{b : v >= t_b} on the same fp32 value the
+reference bins; here that count (numpy emulation of the device rule) is
+compared with the oracle's step-by-step restatement of the reference chain
+over random values, values on and one ulp either side of every threshold,
+and the special values (signed zeros, infinities, NaN, values overflowing
+the reference's int64 conversion).
+"""
+
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from oracle import QuantParams
+from prismkv_b200.tables import build_host_tables
+
+CONFIGS = [(4, 4, 4), (3, 3, 2), (2, 3, 1), (1, 1, 1), (8, 4, 4), (5, 5, 6), (4, 6, 6)]
+
+
+def _kernel_bins(ht, z, x, y):
+    """numpy emulation of the encode kernel's binning (pkv_codec.cu)."""
+    z = np.asarray(z, np.float32)
+    iz = np.searchsorted(ht.z_thr, z, side="right")
+    iz = np.where(z >= np.float32(ht.z_hi), 0, iz)
+    iz = np.where(np.isnan(z), ht.z_nan_bin, iz)
+    with np.errstate(over="ignore", invalid="ignore"):
+        s = (x * x).astype(np.float32) + (y * y).astype(np.float32)
+    ir = np.where(np.isnan(s), 0, np.searchsorted(ht.r2_thr, s, side="right"))
+    th = np.arctan2(y.astype(np.float64), x.astype(np.float64)).astype(np.float32)
+    it = np.where(np.isnan(th), 0, np.searchsorted(ht.th_thr, th, side="right"))
+    return iz, ir, it
+
+
+def _probe_values(thr, scale, rng):
+    thr = thr[np.isfinite(thr)]
+    around = np.concatenate([thr, np.nextafter(thr, np.float32(np.inf)), np.nextafter(thr, np.float32(-np.inf))])
+    specials = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 1e19, -1e19, 1e30, -1e30, 1e-40, 3e38],
+                        dtype=np.float32)
+    rnd = (rng.standard_normal(200000) * scale).astype(np.float32)
+    return np.concatenate([around.astype(np.float32), specials, rnd])
+
+
+@pytest.mark.parametrize("bits", CONFIGS, ids=str)
+def test_encode_thresholds_match_reference_chain(bits):
+    rng = np.random.default_rng(sum(bits))
+    dim = 96
+    p = QuantParams.default(dim, *bits)
+    ht = build_host_tables(dim, *bits, np.eye(dim, dtype=np.float32), p.z_min, p.z_max, p.r_max)
+    z = _probe_values(ht.z_thr, 6.0, rng)
+    iz, _, _ = _kernel_bins(ht, z, np.zeros_like(z), np.zeros_like(z))
+    np.testing.assert_array_equal(iz, oracle.bin_z(z, p))
+    # radius: probe along x with y = 0 and on random (x, y)
+    rt = np.sqrt(ht.r2_thr.astype(np.float64)).astype(np.float32)
+    xv = np.concatenate([_probe_values(rt, 5.0, rng), (rng.standard_normal(100000) * 3).astype(np.float32)])
+    yv = np.concatenate([np.zeros(xv.size - 100000, np.float32), (rng.standard_normal(100000) * 3).astype(np.float32)])
+    _, ir, it = _kernel_bins(ht, np.zeros_like(xv), xv, yv)
+    np.testing.assert_array_equal(ir, oracle.bin_r(oracle.prismkv_oracle.radius_f32(xv, yv), p))
+    th = oracle.prismkv_oracle.atan2_f32(yv, xv)
+    np.testing.assert_array_equal(it, oracle.bin_theta(th, p))
+    # angle thresholds probed directly as angles
+    tv = np.concatenate([ht.th_thr, np.nextafter(ht.th_thr, np.float32(9)), np.nextafter(ht.th_thr, np.float32(-9)),
+                         np.float32([-math.pi, math.pi, 0.0, -0.0])]).astype(np.float32)
+    got = np.searchsorted(ht.th_thr, tv, side="right")
+    np.testing.assert_array_equal(got, oracle.bin_theta(tv, p))
+
+
+def test_lloyd_thresholds_match_bucketize():
+    rng = np.random.default_rng(5)
+    b = np.sort(rng.standard_normal(17).astype(np.float32))
+    b[0], b[-1] = b[0] - 1, b[-1] + 1
+    p = QuantParams.default(96)
+    p.lloyd_boundaries = b
+    p.lloyd_centroids = ((b[:-1] + b[1:]) / 2).astype(np.float32)
+    ht = build_host_tables(96, 4, 4, 4, np.eye(96, dtype=np.float32), p.z_min, p.z_max, p.r_max,
+                           lloyd_boundaries=b, lloyd_centroids=p.lloyd_centroids)
+    z = _probe_values(b, 2.0, rng)
+    iz, _, _ = _kernel_bins(ht, z, np.zeros_like(z), np.zeros_like(z))
+    np.testing.assert_array_equal(iz, oracle.bin_z(z, p))
+
+
+@pytest.mark.parametrize("variant", ["v1", "v1_bias", "lloyd", "learned_bias", "v1_332"])
+def test_decode_tables_match_reference_dequant(variant):
+    rng = np.random.default_rng(11)
+    bits = (3, 3, 2) if variant == "v1_332" else (4, 4, 4)
+    p = QuantParams.default(96, *bits)
+    Cz, K = 1 << bits[0], 1 << (bits[1] + bits[2])
+    if "bias" in variant:
+        p.bias_table = (rng.standard_normal((Cz, 3)) * 0.3).astype(np.float32)   # some entries clip
+        p.bias_delta_z = p.delta_z
+    if variant == "lloyd":
+        bnd = np.sort(rng.standard_normal(Cz + 1).astype(np.float32) * 4)
+        p.lloyd_boundaries = bnd
+        p.lloyd_centroids = ((bnd[:-1] + bnd[1:]) / 2).astype(np.float32)
+    if variant.startswith("learned"):
+        p.codebook = (rng.standard_normal((Cz, K, 2)) * 3).astype(np.float32)
+    ht = build_host_tables(96, *bits, np.eye(96, dtype=np.float32), p.z_min, p.z_max, p.r_max,
+                           codebook=p.codebook, lloyd_boundaries=p.lloyd_boundaries,
+                           lloyd_centroids=p.lloyd_centroids, bias_table=p.bias_table,
+                           bias_delta_z=p.bias_delta_z if p.bias_table is not None else None)
+    total = Cz * K
+    codes = np.arange(total)
+    pad = (-total) % p.m
+    rows = np.concatenate([codes, np.zeros(pad, np.int64)]).reshape(-1, p.m)
+    ref = oracle.dequant_rotated(rows, p).reshape(-1, 3)[:total]
+    bf = bits[1] + bits[2]
+    z = ht.dec_z[codes >> bf]
+    xy = ht.dec_xy.reshape(-1, 2)[codes if ht.xy_per_z else codes & ((1 << bf) - 1)]
+    np.testing.assert_array_equal(z, ref[:, 0])
+    # the tables take cos/sin from torch's vectorised CPU kernels, exactly as the
+    # reference's decode does; the oracle rounds them correctly: <= 1 ulp of cos/sin apart
+    tol = 2.0 ** -21 * p.r_max
+    np.testing.assert_allclose(xy[:, 0], ref[:, 1], atol=tol, rtol=0)
+    np.testing.assert_allclose(xy[:, 1], ref[:, 2], atol=tol, rtol=0)
