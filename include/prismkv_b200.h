@@ -54,6 +54,9 @@ enum {
     PKV_ERR_DEVICE = 6        /* a kernel flagged an error (bounded wait expired)*/
 };
 
+/* ---- codec flags -------------------------------------------------------- */
+#define PKV_CODEC_Z_UNIFORM 1   /* uniform z bins without BiasTable (dec_z affine in i_z) */
+
 /* ---- element types ----------------------------------------------------- */
 enum { PKV_F32 = 0, PKV_BF16 = 1, PKV_F16 = 2 };
 
@@ -66,6 +69,9 @@ enum { PKV_F32 = 0, PKV_BF16 = 1, PKV_F16 = 2 };
  *   codebook (2^bits_z, K, 2) learned (x, y) centroids, K = 2^(bits_r+bits_theta)
  *   dec_z    (2^bits_z)       dequantized z per bin, BiasTable folded in
  *   dec_xy   (xy_per_z ? 2^bits_z * K : K, 2) dequantized (x, y), bias folded in
+ *   bias_xy  (2^bits_z, 2) the clamped BiasTable (x, y) terms alone (NULL when
+ *            there is no BiasTable); the polar attention path subtracts them
+ *            per z-bin instead of reading the per-code dec_xy
  * z_hi: z >= z_hi maps to bin 0 (uniform bins: the reference's int64
  * conversion of an out-of-range floor); NaN when unused.  z_nan_bin: bin of
  * a NaN z (0 for uniform bins, 2^bits_z - 1 for Lloyd-Max boundaries).     */
@@ -76,6 +82,8 @@ typedef struct pkv_codec {
     int32_t xy_per_z;                     /* dec_xy indexed by full code     */
     int32_t z_nan_bin;
     float z_hi;
+    float r_max;                          /* polar grid: r(i_r) = i_r * r_max / (2^bits_r - 1) */
+    int32_t flags;                        /* PKV_CODEC_Z_UNIFORM: dec_z[i] = dec_z[0] + i * step */
     const float *R;                       /* (dim, dim) row-major rotation   */
     const float *z_thr;
     const float *r2_thr;
@@ -83,6 +91,7 @@ typedef struct pkv_codec {
     const float *codebook;
     const float *dec_z;
     const float *dec_xy;
+    const float *bias_xy;                 /* (2^bits_z, 2) clamped BiasTable (x, y), or NULL */
 } pkv_codec;
 
 /* ---- decode attention -------------------------------------------------- *

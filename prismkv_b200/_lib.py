@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(HERE, "libprismkv_b200.so")
 
 PKV_OK = 0
 PKV_F32, PKV_BF16, PKV_F16 = 0, 1, 2
+PKV_CODEC_Z_UNIFORM = 1
 DTYPE_CODES = {torch.float32: PKV_F32, torch.bfloat16: PKV_BF16, torch.float16: PKV_F16}
 
 EXPORTED = ("pkv_abi_version", "pkv_strerror", "pkv_device_error", "pkv_encode", "pkv_decode",
@@ -28,8 +29,9 @@ EXPORTED = ("pkv_abi_version", "pkv_strerror", "pkv_device_error", "pkv_encode",
 class PkvCodec(ctypes.Structure):
     _fields_ = [("dim", c_int32), ("bits_z", c_int32), ("bits_r", c_int32), ("bits_theta", c_int32),
                 ("xy_mode", c_int32), ("xy_per_z", c_int32), ("z_nan_bin", c_int32), ("z_hi", c_float),
+                ("r_max", c_float), ("flags", c_int32),
                 ("R", c_void_p), ("z_thr", c_void_p), ("r2_thr", c_void_p), ("th_thr", c_void_p),
-                ("codebook", c_void_p), ("dec_z", c_void_p), ("dec_xy", c_void_p)]
+                ("codebook", c_void_p), ("dec_z", c_void_p), ("dec_xy", c_void_p), ("bias_xy", c_void_p)]
 
 
 class PkvAttnArgs(ctypes.Structure):

@@ -49,6 +49,7 @@ class DeviceCodec:
         self._cb = up(host.codebook)
         self._dz = up(host.dec_z)
         self._dxy = up(host.dec_xy)
+        self._bxy = up(host.bias_xy) if host.bias_xy is not None else None
         s = _lib.PkvCodec()
         s.dim = host.dim
         s.bits_z, s.bits_r, s.bits_theta = host.bits
@@ -56,6 +57,8 @@ class DeviceCodec:
         s.xy_per_z = host.xy_per_z
         s.z_nan_bin = host.z_nan_bin
         s.z_hi = host.z_hi
+        s.r_max = host.r_max
+        s.flags = _lib.PKV_CODEC_Z_UNIFORM if host.z_uniform else 0
         s.R = self._R.data_ptr()
         s.z_thr = self._z_thr.data_ptr()
         s.r2_thr = self._r2.data_ptr()
@@ -63,6 +66,7 @@ class DeviceCodec:
         s.codebook = self._cb.data_ptr()
         s.dec_z = self._dz.data_ptr()
         s.dec_xy = self._dxy.data_ptr()
+        s.bias_xy = self._bxy.data_ptr() if self._bxy is not None else None
         self.struct = s
         self._ws: Dict[int, torch.Tensor] = {}
         self.R = self._R.view(host.dim, host.dim)

@@ -119,7 +119,7 @@ static int check_attn(const pkv_codec* c, const pkv_attn_args* a) {
     if (!(std::isfinite(a->scale))) return PKV_ERR_INVALID;
     if (a->num_splits < 0) return PKV_ERR_INVALID;
     if (a->batch == 0) return PKV_OK;
-    if (!a->q || !a->k_codes || !a->v_codes) return PKV_ERR_INVALID;
+    if (!a->q || (a->seq_len > 0 && (!a->k_codes || !a->v_codes))) return PKV_ERR_INVALID;
     if (a->partial_only ? !a->partial_out : !a->out) return PKV_ERR_INVALID;
     const int64_t m = c->dim / 3;
     if (a->kv_head_stride < (int64_t)a->seq_len * m || a->kv_batch_stride < 0) return PKV_ERR_INVALID;

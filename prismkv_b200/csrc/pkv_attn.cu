@@ -9,21 +9,25 @@
 // learned codebooks / BiasTable / Lloyd-Max (stacked_plane.py:268-327),
 // because decode = rot_q @ R and R is orthogonal.
 //
-// Layout and schedule:
-//  * codes: (B, Hkv, S, m) of uint8/uint16, one 32/64-byte row per token;
+// Common schedule:
+//  * codes: (B, Hkv, S, m) of uint8/uint16, one m-code row per token;
 //  * one work item = (b, kv head, split) = a contiguous token range;
 //    persistent CTAs take items round-robin;
-//  * warp 4 (producer) streams K and V code tiles of TT tokens into a
-//    STAGES-deep shared-memory ring with 1-D TMA bulk copies completing on
-//    mbarriers; warps 0-3 (consumers) each own 32 tokens of a tile;
-//  * consumer lane j owns triplet j (and j+32): it decodes the code through
-//    the shared-memory LUT and forms partial dot products for every query
-//    head of the group; a 32-way transpose-reduce leaves the full score of
-//    one (head, token) pair in each lane; online softmax in base 2; V is
-//    accumulated per lane in rotated space (no reduction needed);
+//  * a producer warp streams code tiles into a shared-memory ring with 1-D
+//    TMA bulk copies completing on mbarriers; consumer warps own 32 tokens of
+//    a tile each, lane j owning triplet j;
 //  * splits of one (b, kv head) write (m, l, o) partials to the workspace;
 //    the last CTA to finish (atomic counter) merges them, normalises and
 //    applies R once, then resets the counter.
+//
+// Two kernels:
+//  * attn_polar_kernel -- uniform polar (x, y) bins (any z bins, optional
+//    BiasTable): two passes per item (K -> scores in shared memory, exact
+//    max, then V with fixed weights).  K scores come from per-lane tables
+//    indexed by the code fields (one bank per lane: conflict-free), V from a
+//    16-entry (cos, sin) table and the radius index itself.
+//  * attn_lut_kernel -- any codec (learned codebooks): one pass, online
+//    softmax, (z, x, y) from full-code LUTs.
 //
 // Every mbarrier wait is bounded; on expiry the kernel sets the device error
 // word, stops issuing copies, drains what it issued and returns.
@@ -35,9 +39,8 @@
 
 namespace pkv {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kTT = 128;               // tokens per tile (32 per consumer warp)
 constexpr float kLn2 = 0.69314718055994530942f;
+constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnParams {
     int B, Hq, Hkv, S, G, m, dim;
@@ -47,41 +50,17 @@ struct AttnParams {
     const int32_t* seq_lens;
     float scale_log2;
     float* out; int64_t out_bs, out_hs;
-    int nsplit, chunk;                 // chunk: tokens per split, multiple of kTT
+    int nsplit, chunk;                 // chunk: tokens per split, multiple of the tile
     int partial_only; float* partial_out;
     float* ws_part; int32_t* ws_count;
-    const float* R; const float* dec_z; const float* dec_xy;
+    const float* R; const float* dec_z; const float* dec_xy; const float* bias_xy;
+    int bits_z, bits_r, bits_t;
     int bits_flat, code_mask, flat_mask, xy_per_z, n_xy, Cz;
+    float r_max;
     int num_items, stages;
-    float* sm_dummy;
-};
-
-struct SmemLayout {
-    int stage_bytes, stages;
-    int off_stage, off_R, off_xy, off_z, off_q, off_cm, off_cl, off_co, off_fin, off_bar, off_flag, total;
 };
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
-
-__host__ __device__ inline SmemLayout attn_smem_layout(int m, int cb, int dim, int G, int n_xy, int Cz, int stages) {
-    SmemLayout L;
-    L.stages = stages;
-    L.stage_bytes = 2 * kTT * m * cb;
-    int o = 0;
-    L.off_stage = o; o += stages * L.stage_bytes; o = align_up(o, 16);
-    L.off_R = o; o += dim * (dim + 1) * 4; o = align_up(o, 16);
-    L.off_xy = o; o += n_xy * 8; o = align_up(o, 16);
-    L.off_z = o; o += Cz * 4; o = align_up(o, 16);
-    L.off_q = o; o += G * dim * 4; o = align_up(o, 16);
-    L.off_cm = o; o += kConsumerWarps * G * 4;
-    L.off_cl = o; o += kConsumerWarps * G * 4; o = align_up(o, 16);
-    L.off_co = o; o += kConsumerWarps * G * dim * 4; o = align_up(o, 16);
-    L.off_fin = o; o += G * dim * 4; o = align_up(o, 16);
-    L.off_bar = o; o += 2 * stages * 8;
-    L.off_flag = o; o += 16;
-    L.total = o;
-    return L;
-}
 
 __device__ __forceinline__ float q_load(const void* q, int qdt, int64_t idx) {
     if (qdt == PKV_F32) return __ldg(static_cast<const float*>(q) + idx);
@@ -105,7 +84,7 @@ __device__ __forceinline__ ItemRange item_range(const AttnParams& p, int item) {
 }
 
 // transpose-reduce: on entry each lane holds v[0..31]; on exit v[0] of lane l
-// holds sum over all lanes of their v[l].
+// holds the sum over all lanes of their v[l].
 __device__ __forceinline__ void transpose_reduce32(float (&v)[32], int lane) {
     #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
@@ -119,102 +98,795 @@ __device__ __forceinline__ void transpose_reduce32(float (&v)[32], int lane) {
     }
 }
 
-template <int CB, int TPL, int G, bool TMA>
-__global__ void __launch_bounds__(TMA ? 160 : 128) attn_decode_kernel(AttnParams p) {
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    // d = a * b + c on two fp32 lanes (sm_100 paired FMA), operands packed in registers
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// rotated, scaled query of every head of the group -> sQ[G][dim]:
+// sQ[g][k] = scale*log2(e) * sum_i q[g][i] R[k][i].  One warp per output row k,
+// lanes over i (coalesced rows of R), shuffle reduction.
+template <int G>
+__device__ __forceinline__ void rotate_query(const AttnParams& p, const ItemRange& r, const float* Rp, int pitch,
+                                             float* sQ, int tid, int nthr) {
+    const int dim = p.dim, lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
+    float qv[G][6];                                   // dim <= 192: six per lane
+    #pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const int hq = r.hk * p.G + g;
+        const int64_t qb = (int64_t)r.b * p.q_bs + (int64_t)hq * p.q_hs;
+        #pragma unroll
+        for (int u = 0; u < 6; ++u) {
+            const int i = lane + 32 * u;
+            qv[g][u] = (g < p.G && i < dim) ? q_load(p.q, p.qdt, qb + i) : 0.f;
+        }
+    }
+    for (int k = warp; k < dim; k += nw) {
+        float rv[6];
+        #pragma unroll
+        for (int u = 0; u < 6; ++u) {
+            const int i = lane + 32 * u;
+            rv[u] = (i < dim) ? Rp[k * pitch + i] : 0.f;
+        }
+        #pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float acc = 0.f;
+            #pragma unroll
+            for (int u = 0; u < 6; ++u) acc = fmaf(qv[g][u], rv[u], acc);
+            #pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            if (lane == 0) sQ[g * dim + k] = acc * p.scale_log2;
+        }
+    }
+}
+
+// Per-item epilogue shared by both kernels.  Inputs in shared memory, per head
+// g < greal: sM[g] (running max, log2 units), sL[g], sO[g*dim + k] (unnormalised
+// rotated-space output).  Writes the partial row, or merges splits and writes
+// out = (o / l) @ R.  All `nthr` consumer threads call it; barrier id 1.
+__device__ void finish_item(const AttnParams& p, const ItemRange& r, const float* sM, const float* sL,
+                            const float* sO, float* sFin, int* sflag, const float* Rp, int pitch, int tid,
+                            int nthr) {
+    const int dim = p.dim, greal = p.G;
+    const bool single = (p.nsplit == 1);
+    bool finalize = single && !p.partial_only;
+    for (int idx = tid; idx < greal * (dim + 2); idx += nthr) {
+        const int g = idx / (dim + 2), k = idx % (dim + 2);
+        const float M = sM[g], L = sL[g];
+        const int hq = r.hk * greal + g;
+        if (finalize) {
+            if (k >= 2) sFin[g * dim + (k - 2)] = (L > 0.f) ? sO[g * dim + (k - 2)] / L : 0.f;
+        } else {
+            const float val = (k == 0) ? M : (k == 1 ? L : sO[g * dim + (k - 2)]);
+            if (single) {
+                float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
+                dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : val;
+            } else {
+                float* dst = p.ws_part + (((int64_t)r.b * p.Hq + hq) * p.nsplit + r.split) * (dim + 2);
+                dst[k] = val;
+            }
+        }
+    }
+    if (!single) {
+        __threadfence();
+        named_bar_sync(1, nthr);
+        if (tid == 0) {
+            int32_t* cnt = p.ws_count + (r.b * p.Hkv + r.hk);
+            const int prev = atomicAdd(cnt, 1);
+            const int last = (prev == p.nsplit - 1);
+            if (last) { __threadfence(); atomicExch(cnt, 0); }
+            sflag[0] = last;
+        }
+        named_bar_sync(1, nthr);
+        if (sflag[0]) {
+            for (int idx = tid; idx < greal * (dim + 2); idx += nthr) {
+                const int g = idx / (dim + 2), k = idx % (dim + 2);
+                const int hq = r.hk * greal + g;
+                const float* src = p.ws_part + ((int64_t)r.b * p.Hq + hq) * p.nsplit * (dim + 2);
+                float M = -INFINITY;
+                for (int sp = 0; sp < p.nsplit; ++sp) M = fmaxf(M, __ldcg(src + sp * (dim + 2)));
+                float v = 0.f, lsw = 0.f;
+                for (int sp = 0; sp < p.nsplit; ++sp) {
+                    const float ms = __ldcg(src + sp * (dim + 2));
+                    const float f = (ms == -INFINITY) ? 0.f : fast_exp2(ms - M);
+                    lsw = fmaf(__ldcg(src + sp * (dim + 2) + 1), f, lsw);
+                    if (k >= 2) v = fmaf(__ldcg(src + sp * (dim + 2) + k), f, v);
+                }
+                if (p.partial_only) {
+                    float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
+                    dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : (k == 1 ? lsw : v);
+                } else if (k >= 2) {
+                    sFin[g * dim + (k - 2)] = (lsw > 0.f) ? v / lsw : 0.f;
+                }
+            }
+            finalize = !p.partial_only;
+        }
+    }
+    if (finalize) {
+        named_bar_sync(1, nthr);
+        for (int idx = tid; idx < greal * dim; idx += nthr) {
+            const int g = idx / dim, i = idx % dim;
+            float v = 0.f;
+            #pragma unroll 4
+            for (int k = 0; k < dim; ++k) v = fmaf(sFin[g * dim + k], Rp[k * pitch + i], v);
+            const int hq = r.hk * greal + g;
+            p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
+        }
+    }
+    named_bar_sync(1, nthr);     // shared scratch is reused by the next item
+}
+
+// Producer loop: for every item, `passes` sweeps over its token range (K then V
+// for the two-pass kernel; K+V tiles together for the one-pass kernel).
+template <int TT, bool KV_TOGETHER>
+__device__ void produce(const AttnParams& p, uint8_t* stage_base, int stage_bytes, uint64_t* full,
+                        uint64_t* empty, int ncons_warps, int code_bytes) {
+    const uint32_t row_bytes = (uint32_t)(p.m * code_bytes);
+    int seq = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+        const ItemRange r = item_range(p, item);
+        const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.hk * p.kv_hs) * code_bytes;
+        for (int pass = 0; pass < (KV_TOGETHER ? 1 : 2) && ok; ++pass) {
+            for (int t0 = r.tok0; t0 < r.tok1; t0 += TT, ++seq) {
+                const int s = seq % p.stages;
+                const int use = seq / p.stages;
+                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, kErrWaitEmpty)) { ok = false; break; }
+                const int nt = min(TT, r.tok1 - t0);
+                const uint32_t bytes = (uint32_t)nt * row_bytes;
+                uint8_t* dst = stage_base + s * stage_bytes;
+                const int64_t off = base + (int64_t)t0 * row_bytes;
+                if (KV_TOGETHER) {
+                    mbar_arrive_expect_tx(&full[s], 2 * bytes);
+                    bulk_g2s(dst, p.kc + off, bytes, &full[s]);
+                    bulk_g2s(dst + TT * row_bytes, p.vc + off, bytes, &full[s]);
+                } else {
+                    mbar_arrive_expect_tx(&full[s], bytes);
+                    bulk_g2s(dst, (pass == 0 ? p.kc : p.vc) + off, bytes, &full[s]);
+                }
+            }
+        }
+    }
+    const int issued = seq;                           // drain before the CTA may exit
+    for (int q = max(0, issued - p.stages); q < issued; ++q)
+        mbar_wait(&full[q % p.stages], (q / p.stages) & 1, kErrWaitDrain);
+}
+
+// ===========================================================================
+// attn_polar_kernel
+// ===========================================================================
+constexpr int kPW = 8;            // consumer warps
+constexpr int kPTT = 256;         // tokens per tile (32 per consumer warp)
+constexpr int kPChunk = 4096;     // score entries kept per item (all heads of the group)
+
+struct PolarLayout {
+    int stage_bytes, stages, kxy, ct, cz, chunk;
+    int off_stage, off_kt, off_kz, off_vz, off_cs, off_vb, off_q, off_s, off_red, off_acc, off_fin, off_misc,
+        off_bar, total;
+};
+
+__host__ __device__ inline PolarLayout polar_layout(int m, int cb, int dim, int G, int bits_z, int bits_r,
+                                                    int bits_t, int stages) {
+    PolarLayout L;
+    L.stages = stages;
+    L.kxy = 1 << (bits_r + bits_t);
+    L.ct = 1 << bits_t;
+    L.cz = 1 << bits_z;
+    L.chunk = kPChunk / G;
+    L.stage_bytes = kPTT * m * cb;
+    int o = 0;
+    L.off_stage = o; o += stages * L.stage_bytes; o = align_up(o, 128);
+    L.off_kt = o; o += (G == 1 ? L.kxy : G * L.ct) * 32 * 4; o = align_up(o, 128);     // per-lane K tables
+    L.off_kz = o; o += G * L.cz * 32 * 4; o = align_up(o, 128);
+    L.off_vz = o; o += L.cz * 4; o = align_up(o, 128);
+    L.off_cs = o; o += L.ct * 8; o = align_up(o, 128);
+    L.off_vb = o; o += L.cz * 8; o = align_up(o, 16);
+    L.off_q = o; o += G * dim * 4; o = align_up(o, 16);
+    L.off_s = o; o += G * L.chunk * 4; o = align_up(o, 16);
+    L.off_red = o; o += kPW * G * 4 * 2; o = align_up(o, 16);
+    L.off_acc = o; o += kPW * G * dim * 4; o = align_up(o, 16);
+    L.off_fin = o; o += G * dim * 4; o = align_up(o, 16);
+    L.off_misc = o; o += (2 * G + 4) * 4; o = align_up(o, 16);
+    L.off_bar = o; o += 2 * stages * 8;
+    L.total = o;
+    return L;
+}
+
+template <int CB, int G, bool BIAS>
+__global__ void __launch_bounds__(kPW * 32 + 32, 2) attn_polar_kernel(AttnParams p) {
     using CT = typename Code<CB>::T;
     constexpr int TB = 32 / G;                     // tokens per transpose block
-    extern __shared__ __align__(128) uint8_t attn_smem[];
-    uint8_t* smem = attn_smem;
-    const SmemLayout L = attn_smem_layout(p.m, CB, p.dim, G, p.n_xy, p.Cz, p.stages);
+    extern __shared__ __align__(128) uint8_t polar_smem[];
+    uint8_t* smem = polar_smem;
+    const PolarLayout L = polar_layout(p.m, CB, p.dim, G, p.bits_z, p.bits_r, p.bits_t, p.stages);
+    float* kT = reinterpret_cast<float*>(smem + L.off_kt);     // G==1: [kxy][32]; else [G][ct][32]
+    float* kZ = reinterpret_cast<float*>(smem + L.off_kz);     // [G][cz][32]
+    float* vZ = reinterpret_cast<float*>(smem + L.off_vz);     // [cz]
+    float2* vCS = reinterpret_cast<float2*>(smem + L.off_cs);  // [ct]  dr*2^-bt*(cos, sin)
+    float2* vB = reinterpret_cast<float2*>(smem + L.off_vb);   // [cz]  -(bias x, bias y)
+    float* sQ = reinterpret_cast<float*>(smem + L.off_q);      // [G][dim]
+    float* sS = reinterpret_cast<float*>(smem + L.off_s);      // [G][chunk] scores -> weights
+    float* sRed = reinterpret_cast<float*>(smem + L.off_red);  // [kPW][G] x2
+    float* sAcc = reinterpret_cast<float*>(smem + L.off_acc);  // [kPW][G][dim]
+    float* sFin = reinterpret_cast<float*>(smem + L.off_fin);
+    float* sM = reinterpret_cast<float*>(smem + L.off_misc);   // [G]
+    float* sL = sM + G;                                        // [G]
+    int* sflag = reinterpret_cast<int*>(sL + G);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.off_bar);
+    uint64_t* empty = full + p.stages;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int dim = p.dim, m = p.m;
+    const int bf = p.bits_flat, bt = p.bits_t;
+    const uint32_t tmask = (1u << bt) - 1u, fmask = (1u << bf) - 1u;
+    const uint32_t rmask = ((1u << p.bits_r) - 1u) << bt;
+    const uint32_t cmask = (uint32_t)p.code_mask;     // codes index the tables only after masking
+    const float dr = p.r_max / (float)((1 << p.bits_r) - 1);
+
+    // ---- query-independent tables ---------------------------------------
+    for (int i = tid; i < L.cz; i += blockDim.x) {
+        vZ[i] = __ldg(p.dec_z + i);
+        if (BIAS) vB[i] = make_float2(-__ldg(p.bias_xy + 2 * i), -__ldg(p.bias_xy + 2 * i + 1));
+    }
+    for (int i = tid; i < L.ct; i += blockDim.x) {
+        // theta_i = i / (C - 1) * 2 pi - pi (stacked_plane.py:307); scaled so that
+        // (i_r << bits_theta) * vCS = r(i_r) * (cos, sin)
+        const float th = (float)i / (float)(L.ct - 1) * 6.283185307179586f - 3.141592653589793f;
+        const float sc = dr * exp2f((float)-bt);
+        vCS[i] = make_float2(cosf(th) * sc, sinf(th) * sc);
+    }
+    if (tid == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kPW);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kPW) {
+        if (lane == 0) produce<kPTT, false>(p, smem + L.off_stage, L.stage_bytes, full, empty, kPW, CB);
+        return;
+    }
+
+    const int nthr = kPW * 32;
+    const int myh = lane / TB, myt = lane % TB;
+    int seq = 0;
+    bool alive = true;
+    for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
+        const ItemRange r = item_range(p, item);
+        const int ntok = r.tok1 - r.tok0;
+        const int ntiles = (ntok + kPTT - 1) / kPTT;
+        rotate_query<G>(p, r, p.R, dim, sQ, tid, nthr);
+        named_bar_sync(1, nthr);
+        // ---- query tables: one column per lane (bank = lane) ----------------
+        if (G == 1) {
+            for (int idx = tid; idx < L.kxy * 32; idx += nthr) {
+                const int e = idx >> 5, j = idx & 31;
+                float v = 0.f;
+                if (j < m) {
+                    const float fr = (float)((e >> bt) << bt);
+                    const float2 cs = vCS[e & tmask];
+                    v = fr * (sQ[3 * j + 1] * cs.x + sQ[3 * j + 2] * cs.y);
+                }
+                kT[idx] = v;
+            }
+        } else {
+            for (int idx = tid; idx < G * L.ct * 32; idx += nthr) {
+                const int g = idx / (L.ct * 32), e = (idx >> 5) % L.ct, j = idx & 31;
+                float v = 0.f;
+                if (j < m) {
+                    const float2 cs = vCS[e];
+                    v = sQ[g * dim + 3 * j + 1] * cs.x + sQ[g * dim + 3 * j + 2] * cs.y;
+                }
+                kT[idx] = v;
+            }
+        }
+        for (int idx = tid; idx < G * L.cz * 32; idx += nthr) {
+            const int g = idx / (L.cz * 32), e = (idx >> 5) % L.cz, j = idx & 31;
+            float v = 0.f;
+            if (j < m) {
+                v = sQ[g * dim + 3 * j] * vZ[e];
+                if (BIAS) v += sQ[g * dim + 3 * j + 1] * vB[e].x + sQ[g * dim + 3 * j + 2] * vB[e].y;
+            }
+            kZ[idx] = v;
+        }
+        named_bar_sync(1, nthr);
+
+        // ---- pass 1: K codes -> scores --------------------------------------
+        float mx = -INFINITY;                      // this lane's head: myh
+        for (int tile = 0; tile < ntiles; ++tile, ++seq) {
+            const int s = seq % p.stages;
+            if (alive && !mbar_wait(&full[s], (seq / p.stages) & 1, kErrWaitFull)) alive = false;
+            const CT* Kt = reinterpret_cast<const CT*>(smem + L.off_stage + s * L.stage_bytes);
+            const int nt = min(kPTT, ntok - tile * kPTT);
+            if (alive && warp * 32 < nt) {
+                #pragma unroll 1
+                for (int blk = 0; blk < G; ++blk) {
+                    const int tl0 = warp * 32 + blk * TB;
+                    float ps[32];
+                    #pragma unroll
+                    for (int t = 0; t < TB; ++t) {
+                        const uint32_t c = (lane < m) ? ((uint32_t)Kt[(tl0 + t) * m + lane] & cmask) : 0u;
+                        if (G == 1) {
+                            ps[t] = kT[((c & fmask) << 5) + lane] + kZ[((c >> bf) << 5) + lane];
+                        } else {
+                            const float fr = __int_as_float((c & rmask) | 0x4B000000u) - 8388608.f;
+                            const uint32_t ti = ((c & tmask) << 5) + lane, zi = ((c >> bf) << 5) + lane;
+                            #pragma unroll
+                            for (int g = 0; g < G; ++g)
+                                ps[g * TB + t] = fmaf(fr, kT[g * L.ct * 32 + ti], kZ[g * L.cz * 32 + zi]);
+                        }
+                    }
+                    transpose_reduce32(ps, lane);
+                    const int tok = tl0 + myt;
+                    if (tok < nt && myh < p.G) {
+                        sS[myh * L.chunk + tile * kPTT + tok] = ps[0];
+                        mx = fmaxf(mx, ps[0]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // ---- exact max per head, weights, l -----------------------------------
+        #pragma unroll
+        for (int off = TB / 2; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        if (myt == 0) sRed[warp * G + myh] = mx;
+        named_bar_sync(1, nthr);
+        if (tid < G) {
+            float M = -INFINITY;
+            for (int w = 0; w < kPW; ++w) M = fmaxf(M, sRed[w * G + tid]);
+            sM[tid] = M;
+        }
+        named_bar_sync(1, nthr);
+        {
+            const int span = ntiles * kPTT;
+            float lp[G];
+            #pragma unroll
+            for (int g = 0; g < G; ++g) {
+                lp[g] = 0.f;
+                const float M = sM[g];
+                for (int t = tid; t < span; t += nthr) {
+                    const float pv = (t < ntok && M != -INFINITY) ? fast_exp2(sS[g * L.chunk + t] - M) : 0.f;
+                    sS[g * L.chunk + t] = pv;
+                    lp[g] += pv;
+                }
+                #pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) lp[g] += __shfl_xor_sync(0xffffffffu, lp[g], off);
+                if (lane == 0) sRed[kPW * G + warp * G + g] = lp[g];
+            }
+        }
+        named_bar_sync(1, nthr);
+        if (tid < G) {
+            float l = 0.f;
+            for (int w = 0; w < kPW; ++w) l += sRed[kPW * G + w * G + tid];
+            sL[tid] = l;
+        }
+
+        // ---- pass 2: V codes, fixed weights -----------------------------------
+        float2 axy[G];
+        float az[G];
+        #pragma unroll
+        for (int g = 0; g < G; ++g) { axy[g] = make_float2(0.f, 0.f); az[g] = 0.f; }
+        for (int tile = 0; tile < ntiles; ++tile, ++seq) {
+            const int s = seq % p.stages;
+            if (alive && !mbar_wait(&full[s], (seq / p.stages) & 1, kErrWaitFull)) alive = false;
+            const CT* Vt = reinterpret_cast<const CT*>(smem + L.off_stage + s * L.stage_bytes);
+            const int nt = min(kPTT, ntok - tile * kPTT);
+            if (alive && warp * 32 < nt && lane < m) {
+                const float* pw = sS + tile * kPTT + warp * 32;
+                #pragma unroll 8
+                for (int t = 0; t < 32; ++t) {
+                    const uint32_t c = (uint32_t)Vt[(warp * 32 + t) * m + lane] & cmask;
+                    const float z = vZ[c >> bf];
+                    const float2 cs = vCS[c & tmask];
+                    const float fr = __int_as_float((c & rmask) | 0x4B000000u) - 8388608.f;
+                    float2 b2;
+                    if (BIAS) b2 = vB[c >> bf];
+                    #pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const float pg = pw[g * L.chunk + t];
+                        az[g] = fmaf(pg, z, az[g]);
+                        const float w = pg * fr;
+                        axy[g] = ffma2(make_float2(w, w), cs, axy[g]);
+                        if (BIAS) axy[g] = ffma2(make_float2(pg, pg), b2, axy[g]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // ---- merge warps --------------------------------------------------------
+        if (lane < m) {
+            #pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float* o = sAcc + (warp * G + g) * dim + 3 * lane;
+                o[0] = az[g]; o[1] = axy[g].x; o[2] = axy[g].y;
+            }
+        }
+        named_bar_sync(1, nthr);
+        for (int idx = tid; idx < G * dim; idx += nthr) {
+            float v = 0.f;
+            #pragma unroll
+            for (int w = 0; w < kPW; ++w) v += sAcc[w * G * dim + idx];
+            sAcc[idx] = v;                      // warp 0's slot now holds the sum
+        }
+        named_bar_sync(1, nthr);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, dim, tid, nthr);
+    }
+}
+
+// ===========================================================================
+// attn_mha12_kernel -- the MHA, head_dim 96, 12-bit (4+4+4) uniform-polar case
+// ===========================================================================
+// Same two-pass schedule as attn_polar_kernel, with the hot loops laid out for
+// the shared-memory data path (one 128-byte wavefront per clock per SM):
+//  * K: lane l reads one 32-bit word = the codes of triplets 2(l%16), 2(l%16)+1
+//    of token t + l/16, so one warp load covers two tokens (128 bytes).  The
+//    score table row e holds, in word w < 16, q'_(2w) . (x, y)(e) and in word
+//    16 + w, q'_(2w+1) . (x, y)(e); lanes of the upper half take their odd
+//    triplet first, so both lookups of a step hit 32 distinct banks.  z enters
+//    through the code bits themselves (uniform bins are affine in i_z).  A
+//    16-lane transpose-reduce completes the scores.
+//  * V: lane l reads 16 bytes = 8 codes of token l/4 (triplets 8(l%4)..+7),
+//    one warp load covers 8 tokens (512 bytes); z and r come from the code
+//    bits, (cos, sin) from a 16-entry table (one wavefront for any pattern).
+namespace mha12 {
+constexpr int W = 8;                                   // consumer warps
+constexpr int TT = 256;                                // tokens per tile (32 per warp)
+constexpr int CH = 4096;                               // tokens per item (scores in smem)
+constexpr int STAGES = 3;
+constexpr int TILE = TT * 64;                          // 32 codes x 2 bytes per token
+constexpr int OFF_KT = STAGES * TILE;                  // [256][32] floats
+constexpr int OFF_CS = OFF_KT + 256 * 32 * 4;          // [16] float2
+constexpr int OFF_Q = OFF_CS + 16 * 8;                 // [96]
+constexpr int OFF_S = OFF_Q + 96 * 4 + 128;            // [CH]
+constexpr int OFF_RED = OFF_S + CH * 4;                // [2][W]
+constexpr int OFF_ACC = OFF_RED + 2 * W * 4;           // [W][96]
+constexpr int OFF_FIN = OFF_ACC + W * 96 * 4;          // [96]
+constexpr int OFF_MISC = OFF_FIN + 96 * 4;             // sM, sL, C, flag
+constexpr int OFF_BAR = OFF_MISC + 64;
+constexpr int TOTAL = OFF_BAR + 2 * STAGES * 8;
+constexpr float MAGIC = 8388608.f;                     // 2^23
+}  // namespace mha12
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// 16-lane transpose-reduce within each half-warp: on exit v[0] of lane l holds
+// the sum over the 16 lanes of its half of their v[l % 16].
+__device__ __forceinline__ void transpose_reduce16(float (&v)[16], int lane) {
+    #pragma unroll
+    for (int off = 8; off >= 1; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+        #pragma unroll
+        for (int i = 0; i < off; ++i) {
+            float send = upper ? v[i] : v[i + off];
+            float keep = upper ? v[i + off] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnParams p) {
+    using namespace mha12;
+    extern __shared__ __align__(128) uint8_t mha12_smem[];
+    uint8_t* smem = mha12_smem;
+    float* kT = reinterpret_cast<float*>(smem + OFF_KT);
+    float2* vCS = reinterpret_cast<float2*>(smem + OFF_CS);
+    float* sQ = reinterpret_cast<float*>(smem + OFF_Q);
+    float* sS = reinterpret_cast<float*>(smem + OFF_S);
+    float* sRed = reinterpret_cast<float*>(smem + OFF_RED);
+    float* sAcc = reinterpret_cast<float*>(smem + OFF_ACC);
+    float* sFin = reinterpret_cast<float*>(smem + OFF_FIN);
+    float* sM = reinterpret_cast<float*>(smem + OFF_MISC);
+    float* sL = sM + 1;
+    float* sC = sM + 2;
+    int* sflag = reinterpret_cast<int*>(sM + 3);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* empty = full + STAGES;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float dr = p.r_max / 15.f;
+    const float z0 = __ldg(p.dec_z), dz = __ldg(p.dec_z + 1) - z0;     // uniform z bins: z = z0 + i dz
+
+    if (tid < 16) {
+        // theta_i = i / 15 * 2 pi - pi (stacked_plane.py:307), scaled so that (i_r << 4) * vCS = r (cos, sin)
+        const float th = (float)tid / 15.f * 6.283185307179586f - 3.141592653589793f;
+        vCS[tid] = make_float2(cosf(th) * dr * 0.0625f, sinf(th) * dr * 0.0625f);
+    }
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], W);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == W) {
+        if (lane == 0) produce<TT, false>(p, smem, TILE, full, empty, W, 2);
+        return;
+    }
+
+    constexpr int nthr = W * 32;
+    const int half = lane >> 4, l16 = lane & 15;
+    const int sh1 = half << 4, sh2 = 16 - sh1;          // which code of the word comes first
+    const int wcol1 = lane, wcol2 = lane ^ 16;           // table words of the first / second code
+    const int tg = lane >> 2, q4 = lane & 3;             // V: token-in-8, 8-triplet chunk
+    int seq = 0;
+    bool alive = true;
+    for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
+        const ItemRange r = item_range(p, item);
+        const int ntok = r.tok1 - r.tok0;
+        const int ntiles = (ntok + TT - 1) / TT;
+        rotate_query<1>(p, r, p.R, 96, sQ, tid, nthr);
+        named_bar_sync(1, nthr);
+        // score table: row e = (i_r << 4) | i_theta; word w < 16 -> triplet 2w, w >= 16 -> 2(w-16)+1
+        for (int idx = tid; idx < 256 * 32; idx += nthr) {
+            const int e = idx >> 5, w = idx & 31;
+            const int j = (w < 16) ? 2 * w : 2 * (w - 16) + 1;
+            const float2 cs = vCS[e & 15];
+            const float fr = (float)(e & 0xF0);
+            kT[idx] = fr * (sQ[3 * j + 1] * cs.x + sQ[3 * j + 2] * cs.y);
+        }
+        if (warp == 0) {                                   // C = z0 * sum_j q'_z,j
+            float c = sQ[3 * lane];
+            #pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+            if (lane == 0) sC[0] = c * z0;
+        }
+        named_bar_sync(1, nthr);
+        // z coefficient per code of this lane: q'_z,j * dz / 256 (the code bits give 256 i_z)
+        const int j1 = 2 * l16 + half, j2 = 2 * l16 + 1 - half;
+        const float2 az = make_float2(sQ[3 * j1] * dz * (1.f / 256.f), sQ[3 * j2] * dz * (1.f / 256.f));
+        const float C = sC[0];
+
+        // ---- pass 1: K -> scores ------------------------------------------------
+        float mx = -INFINITY;
+        for (int tile = 0; tile < ntiles; ++tile, ++seq) {
+            const int s = seq % STAGES;
+            if (alive && !mbar_wait(&full[s], (seq / STAGES) & 1, kErrWaitFull)) alive = false;
+            const uint32_t* K32 = reinterpret_cast<const uint32_t*>(smem + s * TILE);
+            const int nt = min(TT, ntok - tile * TT);
+            if (alive && warp * 32 < nt) {
+                float ps[16];
+                #pragma unroll
+                for (int st = 0; st < 16; ++st) {
+                    const uint32_t w = K32[(warp * 32 + 2 * st + half) * 16 + l16];
+                    const uint32_t c1 = w >> sh1, c2 = w >> sh2;
+                    const float2 zz = fadd2(make_float2(__int_as_float((c1 & 0xF00u) | 0x4B000000u),
+                                                        __int_as_float((c2 & 0xF00u) | 0x4B000000u)),
+                                            make_float2(-MAGIC, -MAGIC));
+                    const float t1 = kT[((c1 & 0xFFu) << 5) + wcol1];
+                    const float t2 = kT[((c2 & 0xFFu) << 5) + wcol2];
+                    const float2 a = ffma2(az, zz, make_float2(t1, t2));
+                    ps[st] = a.x + a.y;
+                }
+                transpose_reduce16(ps, lane);
+                const int tok = warp * 32 + 2 * l16 + half;
+                if (tok < nt) {
+                    const float sc = ps[0] + C;
+                    sS[tile * TT + tok] = sc;
+                    mx = fmaxf(mx, sc);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        #pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        if (lane == 0) sRed[warp] = mx;
+        named_bar_sync(1, nthr);
+        float M = -INFINITY;
+        #pragma unroll
+        for (int w = 0; w < W; ++w) M = fmaxf(M, sRed[w]);
+        // ---- weights ------------------------------------------------------------
+        float lp = 0.f;
+        for (int t = tid; t < ntiles * TT; t += nthr) {
+            const float pv = (t < ntok && M != -INFINITY) ? fast_exp2(sS[t] - M) : 0.f;
+            sS[t] = pv;
+            lp += pv;
+        }
+        #pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) lp += __shfl_xor_sync(0xffffffffu, lp, off);
+        if (lane == 0) sRed[W + warp] = lp;
+        named_bar_sync(1, nthr);
+        if (tid == 0) {
+            float l = 0.f;
+            for (int w = 0; w < W; ++w) l += sRed[W + w];
+            sL[0] = l;
+            sM[0] = M;
+        }
+
+        // ---- pass 2: V with fixed weights ---------------------------------------
+        float2 axy[8], azz[4];
+        #pragma unroll
+        for (int k = 0; k < 8; ++k) axy[k] = make_float2(0.f, 0.f);
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) azz[k] = make_float2(0.f, 0.f);
+        const uint32_t csb = (uint32_t)__cvta_generic_to_shared(vCS);
+        for (int tile = 0; tile < ntiles; ++tile, ++seq) {
+            const int s = seq % STAGES;
+            if (alive && !mbar_wait(&full[s], (seq / STAGES) & 1, kErrWaitFull)) alive = false;
+            const uint4* V16 = reinterpret_cast<const uint4*>(smem + s * TILE);
+            const int nt = min(TT, ntok - tile * TT);
+            if (alive && warp * 32 < nt) {
+                #pragma unroll
+                for (int st = 0; st < 4; ++st) {
+                    const int tok = warp * 32 + 8 * st + tg;
+                    const uint4 wv = V16[tok * 4 + q4];
+                    const float pw = sS[tile * TT + tok];
+                    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+                    #pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        const uint32_t w = ww[h];
+                        // low code (triplet 8 q4 + 2h), high code (8 q4 + 2h + 1)
+                        const float2 zf = fadd2(make_float2(__int_as_float((w & 0xF00u) | 0x4B000000u),
+                                                            __int_as_float(__byte_perm(w, 0x4B000000u, 0x7534))),
+                                                make_float2(-MAGIC, -MAGIC));
+                        const float2 rf = fadd2(make_float2(__int_as_float((w & 0xF0u) | 0x4B000000u),
+                                                            __int_as_float(((w >> 16) & 0xF0u) | 0x4B000000u)),
+                                                make_float2(-MAGIC, -MAGIC));
+                        float2 cs0, cs1;
+                        asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(cs0.x), "=f"(cs0.y)
+                                     : "r"(csb + ((w << 3) & 0x78u)));
+                        asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(cs1.x), "=f"(cs1.y)
+                                     : "r"(csb + ((w >> 13) & 0x78u)));
+                        azz[h] = ffma2(make_float2(pw, pw), zf, azz[h]);
+                        const float w0 = pw * rf.x, w1 = pw * rf.y;
+                        axy[2 * h] = ffma2(make_float2(w0, w0), cs0, axy[2 * h]);
+                        axy[2 * h + 1] = ffma2(make_float2(w1, w1), cs1, axy[2 * h + 1]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // reduce over the 8 token groups of the warp (lanes sharing q4)
+        #pragma unroll
+        for (int off = 4; off <= 16; off <<= 1) {
+            #pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                axy[k].x += __shfl_xor_sync(0xffffffffu, axy[k].x, off);
+                axy[k].y += __shfl_xor_sync(0xffffffffu, axy[k].y, off);
+            }
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                azz[k].x += __shfl_xor_sync(0xffffffffu, azz[k].x, off);
+                azz[k].y += __shfl_xor_sync(0xffffffffu, azz[k].y, off);
+            }
+        }
+        if (tg == 0) {
+            float* o = sAcc + warp * 96 + 24 * q4;          // triplets 8 q4 .. 8 q4 + 7
+            #pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                o[6 * h + 0] = azz[h].x;  o[6 * h + 1] = axy[2 * h].x;      o[6 * h + 2] = axy[2 * h].y;
+                o[6 * h + 3] = azz[h].y;  o[6 * h + 4] = axy[2 * h + 1].x;  o[6 * h + 5] = axy[2 * h + 1].y;
+            }
+        }
+        named_bar_sync(1, nthr);
+        if (tid < 96) {
+            float v = 0.f;
+            #pragma unroll
+            for (int w = 0; w < W; ++w) v += sAcc[w * 96 + tid];
+            // z: sum p (z0 + dz i_z) = z0 l + dz/256 * sum p (256 i_z)
+            if (tid % 3 == 0) v = fmaf(z0, sL[0], v * dz * (1.f / 256.f));
+            sAcc[tid] = v;
+        }
+        named_bar_sync(1, nthr);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, 96, tid, nthr);
+    }
+}
+
+// ===========================================================================
+// attn_lut_kernel (any codec)
+// ===========================================================================
+constexpr int kLW = 4;             // consumer warps
+constexpr int kLTT = 128;          // tokens per tile (32 per consumer warp)
+
+struct LutLayout {
+    int stage_bytes, stages;
+    int off_stage, off_R, off_xy, off_z, off_q, off_cm, off_cl, off_co, off_fin, off_misc, off_bar, total;
+};
+
+__host__ __device__ inline LutLayout lut_layout(int m, int cb, int dim, int G, int n_xy, int Cz, int stages) {
+    LutLayout L;
+    L.stages = stages;
+    L.stage_bytes = 2 * kLTT * m * cb;
+    int o = 0;
+    L.off_stage = o; o += stages * L.stage_bytes; o = align_up(o, 16);
+    L.off_R = o; o += dim * (dim + 1) * 4; o = align_up(o, 16);
+    L.off_xy = o; o += n_xy * 8; o = align_up(o, 16);
+    L.off_z = o; o += Cz * 4; o = align_up(o, 16);
+    L.off_q = o; o += G * dim * 4; o = align_up(o, 16);
+    L.off_cm = o; o += kLW * G * 4;
+    L.off_cl = o; o += kLW * G * 4; o = align_up(o, 16);
+    L.off_co = o; o += kLW * G * dim * 4; o = align_up(o, 16);
+    L.off_fin = o; o += G * dim * 4; o = align_up(o, 16);
+    L.off_misc = o; o += (3 * G + 4) * 4 + G * dim * 4; o = align_up(o, 16);
+    L.off_bar = o; o += 2 * stages * 8;
+    L.total = o;
+    return L;
+}
+
+template <int CB, int TPL, int G, bool TMA>
+__global__ void __launch_bounds__(TMA ? kLW * 32 + 32 : kLW * 32) attn_lut_kernel(AttnParams p) {
+    using CT = typename Code<CB>::T;
+    constexpr int TB = 32 / G;
+    extern __shared__ __align__(128) uint8_t lut_smem[];
+    uint8_t* smem = lut_smem;
+    const LutLayout L = lut_layout(p.m, CB, p.dim, G, p.n_xy, p.Cz, p.stages);
     float* sR = reinterpret_cast<float*>(smem + L.off_R);          // R[k][i], pitch dim+1
     const float2* sXY = reinterpret_cast<const float2*>(smem + L.off_xy);
     const float* sZ = reinterpret_cast<const float*>(smem + L.off_z);
-    float* sQ = reinterpret_cast<float*>(smem + L.off_q);          // [G][dim]
-    float* sCm = reinterpret_cast<float*>(smem + L.off_cm);        // [4][G]
-    float* sCl = reinterpret_cast<float*>(smem + L.off_cl);        // [4][G]
-    float* sCo = reinterpret_cast<float*>(smem + L.off_co);        // [4][G][dim]
-    float* sFin = reinterpret_cast<float*>(smem + L.off_fin);      // [G][dim]
+    float* sQ = reinterpret_cast<float*>(smem + L.off_q);
+    float* sCm = reinterpret_cast<float*>(smem + L.off_cm);
+    float* sCl = reinterpret_cast<float*>(smem + L.off_cl);
+    float* sCo = reinterpret_cast<float*>(smem + L.off_co);
+    float* sFin = reinterpret_cast<float*>(smem + L.off_fin);
+    float* sM = reinterpret_cast<float*>(smem + L.off_misc);
+    float* sL = sM + G;
+    int* sflag = reinterpret_cast<int*>(sL + G);
+    float* sO = reinterpret_cast<float*>(smem + L.off_misc) + 3 * G + 4;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.off_bar);
     uint64_t* empty = full + p.stages;
-    int* sflag = reinterpret_cast<int*>(smem + L.off_flag);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int dim = p.dim, m = p.m, pitch = dim + 1;
-    const int nthreads = blockDim.x;
 
-    // ---- prologue: R, LUTs, barriers --------------------------------------
-    for (int idx = tid; idx < dim * dim; idx += nthreads) {
+    for (int idx = tid; idx < dim * dim; idx += blockDim.x) {
         int k = idx / dim, i = idx % dim;
         sR[k * pitch + i] = __ldg(p.R + idx);
     }
     {
         float2* xy = reinterpret_cast<float2*>(smem + L.off_xy);
         const float2* g = reinterpret_cast<const float2*>(p.dec_xy);
-        for (int idx = tid; idx < p.n_xy; idx += nthreads) xy[idx] = __ldg(g + idx);
+        for (int idx = tid; idx < p.n_xy; idx += blockDim.x) xy[idx] = __ldg(g + idx);
         float* z = reinterpret_cast<float*>(smem + L.off_z);
-        for (int idx = tid; idx < p.Cz; idx += nthreads) z[idx] = __ldg(p.dec_z + idx);
+        for (int idx = tid; idx < p.Cz; idx += blockDim.x) z[idx] = __ldg(p.dec_z + idx);
     }
     if (TMA && tid == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
+            mbar_init(&empty[s], kLW);
         }
         fence_mbar_init();
     }
-    if (tid == 0) sflag[1] = 0;                    // sticky abort flag for this CTA
     __syncthreads();
 
-    // ---- producer warp ------------------------------------------------------
-    if (TMA && warp == kConsumerWarps) {
-        if (lane == 0) {
-            const uint32_t row_bytes = (uint32_t)(m * CB);
-            int seq = 0;
-            bool ok = true;
-            for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
-                ItemRange r = item_range(p, item);
-                const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.hk * p.kv_hs) * CB;
-                for (int t0 = r.tok0; t0 < r.tok1; t0 += kTT, ++seq) {
-                    const int s = seq % p.stages;
-                    const int use = seq / p.stages;
-                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, kErrWaitEmpty)) { ok = false; break; }
-                    const int nt = min(kTT, r.tok1 - t0);
-                    const uint32_t bytes = (uint32_t)nt * row_bytes;
-                    uint8_t* dk = smem + L.off_stage + s * L.stage_bytes;
-                    uint8_t* dv = dk + kTT * row_bytes;
-                    mbar_arrive_expect_tx(&full[s], 2 * bytes);
-                    bulk_g2s(dk, p.kc + base + (int64_t)t0 * row_bytes, bytes, &full[s]);
-                    bulk_g2s(dv, p.vc + base + (int64_t)t0 * row_bytes, bytes, &full[s]);
-                }
-            }
-            // drain: every issued copy must land before the CTA may exit
-            const int issued = seq;
-            for (int q = max(0, issued - p.stages); q < issued; ++q)
-                mbar_wait(&full[q % p.stages], (q / p.stages) & 1, kErrWaitDrain);
-        }
+    if (TMA && warp == kLW) {
+        if (lane == 0) produce<kLTT, true>(p, smem + L.off_stage, L.stage_bytes, full, empty, kLW, CB);
         return;
     }
 
-    // ---- consumers ----------------------------------------------------------
+    const int nthr = kLW * 32;
     const int myh = lane / TB, myt = lane % TB;
     int seq = 0;
     bool alive = true;
     for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
         const ItemRange r = item_range(p, item);
         const int greal = p.G;
-        // rotated, scaled query of every head of the group -> sQ
-        for (int idx = tid; idx < G * dim; idx += kConsumerWarps * 32) {
-            int g = idx / dim, k = idx % dim;
-            float acc = 0.f;
-            if (g < greal) {
-                const int hq = r.hk * greal + g;
-                const int64_t qb = (int64_t)r.b * p.q_bs + (int64_t)hq * p.q_hs;
-                #pragma unroll 4
-                for (int i = 0; i < dim; ++i) acc = fmaf(q_load(p.q, p.qdt, qb + i), sR[k * pitch + i], acc);
-            }
-            sQ[idx] = acc * p.scale_log2;
-        }
-        named_bar_sync(1, kConsumerWarps * 32);
+        rotate_query<G>(p, r, sR, pitch, sQ, tid, nthr);
+        named_bar_sync(1, nthr);
         float qv[G][TPL][3];
         #pragma unroll
         for (int g = 0; g < G; ++g)
@@ -233,26 +905,26 @@ __global__ void __launch_bounds__(TMA ? 160 : 128) attn_decode_kernel(AttnParams
             for (int tp = 0; tp < TPL; ++tp) acc[g][tp][0] = acc[g][tp][1] = acc[g][tp][2] = 0.f;
         }
         float lrun = 0.f;
-        const int64_t base = (int64_t)r.b * p.kv_bs + (int64_t)r.hk * p.kv_hs;   // codes
+        const int64_t base = (int64_t)r.b * p.kv_bs + (int64_t)r.hk * p.kv_hs;
 
-        for (int t0 = r.tok0; t0 < r.tok1; t0 += kTT, ++seq) {
+        for (int t0 = r.tok0; t0 < r.tok1; t0 += kLTT, ++seq) {
             const int s = seq % p.stages;
             const CT* Kt;
             const CT* Vt;
             if (TMA) {
                 if (alive && !mbar_wait(&full[s], (seq / p.stages) & 1, kErrWaitFull)) alive = false;
                 Kt = reinterpret_cast<const CT*>(smem + L.off_stage + s * L.stage_bytes);
-                Vt = Kt + kTT * m;
+                Vt = Kt + kLTT * m;
             } else {
                 Kt = reinterpret_cast<const CT*>(p.kc) + base + (int64_t)t0 * m;
                 Vt = reinterpret_cast<const CT*>(p.vc) + base + (int64_t)t0 * m;
             }
-            const int nt = min(kTT, r.tok1 - t0);
+            const int nt = min(kLTT, r.tok1 - t0);
             if (alive) {
                 #pragma unroll 1
                 for (int blk = 0; blk < 32 / TB; ++blk) {
-                    const int tl0 = warp * 32 + blk * TB;      // first token of block in tile
-                    if (tl0 >= nt) break;                      // warp-uniform
+                    const int tl0 = warp * 32 + blk * TB;
+                    if (tl0 >= nt) break;
                     float ps[32];
                     #pragma unroll
                     for (int t = 0; t < TB; ++t) {
@@ -288,8 +960,8 @@ __global__ void __launch_bounds__(TMA ? 160 : 128) attn_decode_kernel(AttnParams
                     #pragma unroll
                     for (int g = 0; g < G; ++g) {
                         const float mn = fmaxf(mrun[g], __shfl_sync(0xffffffffu, bm, g * TB));
-                        if (mn != mrun[g]) {                   // warp-uniform
-                            const float alpha = fast_exp2(mrun[g] - mn);   // 0 when mrun = -inf
+                        if (mn != mrun[g]) {
+                            const float alpha = fast_exp2(mrun[g] - mn);
                             #pragma unroll
                             for (int tp = 0; tp < TPL; ++tp) {
                                 acc[g][tp][0] *= alpha; acc[g][tp][1] *= alpha; acc[g][tp][2] *= alpha;
@@ -303,7 +975,6 @@ __global__ void __launch_bounds__(TMA ? 160 : 128) attn_decode_kernel(AttnParams
                     for (int g = 1; g < G; ++g) if (g == myh) mine_m = mrun[g];
                     const float pr = valid ? fast_exp2(sc - mine_m) : 0.f;
                     lrun = lrun * alpha_mine + pr;
-                    // V
                     #pragma unroll
                     for (int t = 0; t < TB; ++t) {
                         float pg[G];
@@ -337,7 +1008,7 @@ __global__ void __launch_bounds__(TMA ? 160 : 128) attn_decode_kernel(AttnParams
             }
         }
 
-        // ---- per-item epilogue: merge the 4 consumer warps ---------------------
+        // merge the consumer warps (online-softmax states) into sM / sL / sO
         float lsum = lrun;
         #pragma unroll
         for (int off = TB / 2; off >= 1; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
@@ -354,89 +1025,23 @@ __global__ void __launch_bounds__(TMA ? 160 : 128) attn_decode_kernel(AttnParams
                 }
             }
         }
-        named_bar_sync(1, kConsumerWarps * 32);
-        const bool single = (p.nsplit == 1);
-        // merge warps: (g, k) pairs; write partial row or normalised result
-        for (int idx = tid; idx < G * (dim + 2); idx += kConsumerWarps * 32) {
-            const int g = idx / (dim + 2), k = idx % (dim + 2);
-            if (g >= greal) continue;
+        named_bar_sync(1, nthr);
+        for (int idx = tid; idx < greal * (dim + 1); idx += nthr) {
+            const int g = idx / (dim + 1), k = idx % (dim + 1);
             float M = -INFINITY;
             #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sCm[w * G + g]);
-            float v = 0.f, lsw = 0.f;
+            for (int w = 0; w < kLW; ++w) M = fmaxf(M, sCm[w * G + g]);
+            float v = 0.f;
             #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) {
+            for (int w = 0; w < kLW; ++w) {
                 const float mw = sCm[w * G + g];
                 const float f = (mw == -INFINITY) ? 0.f : fast_exp2(mw - M);
-                lsw = fmaf(sCl[w * G + g], f, lsw);
-                if (k >= 2) v = fmaf(sCo[(w * G + g) * dim + (k - 2)], f, v);
+                v = fmaf(k == dim ? sCl[w * G + g] : sCo[(w * G + g) * dim + k], f, v);
             }
-            const int hq = r.hk * greal + g;
-            if (single && !p.partial_only) {
-                if (k >= 2) sFin[g * dim + (k - 2)] = (lsw > 0.f) ? v / lsw : 0.f;
-            } else {
-                const float val = (k == 0) ? M : (k == 1 ? lsw : v);
-                if (single) {
-                    float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
-                    dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : val;
-                } else {
-                    float* dst = p.ws_part + (((int64_t)r.b * p.Hq + hq) * p.nsplit + r.split) * (dim + 2);
-                    dst[k] = val;                                     // log2-domain max
-                }
-            }
+            if (k == dim) { sL[g] = v; sM[g] = M; } else { sO[g * dim + k] = v; }
         }
-        bool finalize = single && !p.partial_only;
-        bool merge_splits = false;
-        if (!single) {
-            __threadfence();
-            named_bar_sync(1, kConsumerWarps * 32);
-            if (tid == 0) {
-                int32_t* cnt = p.ws_count + (r.b * p.Hkv + r.hk);
-                const int prev = atomicAdd(cnt, 1);
-                const int last = (prev == p.nsplit - 1);
-                if (last) { __threadfence(); atomicExch(cnt, 0); }
-                sflag[0] = last;
-            }
-            named_bar_sync(1, kConsumerWarps * 32);
-            merge_splits = sflag[0] != 0;
-            if (merge_splits) {
-                for (int idx = tid; idx < G * (dim + 2); idx += kConsumerWarps * 32) {
-                    const int g = idx / (dim + 2), k = idx % (dim + 2);
-                    if (g >= greal) continue;
-                    const int hq = r.hk * greal + g;
-                    const float* src = p.ws_part + ((int64_t)r.b * p.Hq + hq) * p.nsplit * (dim + 2);
-                    float M = -INFINITY;
-                    for (int sp = 0; sp < p.nsplit; ++sp) M = fmaxf(M, __ldcg(src + sp * (dim + 2)));
-                    float v = 0.f, lsw = 0.f;
-                    for (int sp = 0; sp < p.nsplit; ++sp) {
-                        const float ms = __ldcg(src + sp * (dim + 2));
-                        const float f = (ms == -INFINITY) ? 0.f : fast_exp2(ms - M);
-                        lsw = fmaf(__ldcg(src + sp * (dim + 2) + 1), f, lsw);
-                        if (k >= 2) v = fmaf(__ldcg(src + sp * (dim + 2) + k), f, v);
-                    }
-                    if (p.partial_only) {
-                        float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
-                        dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : (k == 1 ? lsw : v);
-                    } else if (k >= 2) {
-                        sFin[g * dim + (k - 2)] = (lsw > 0.f) ? v / lsw : 0.f;
-                    }
-                }
-                finalize = !p.partial_only;
-            }
-        }
-        if (finalize) {
-            named_bar_sync(1, kConsumerWarps * 32);
-            // out = fin @ R   (R[k][i], pitch dim+1: lanes over i are conflict-free)
-            for (int idx = tid; idx < greal * dim; idx += kConsumerWarps * 32) {
-                const int g = idx / dim, i = idx % dim;
-                float v = 0.f;
-                #pragma unroll 4
-                for (int k = 0; k < dim; ++k) v = fmaf(sFin[g * dim + k], sR[k * pitch + i], v);
-                const int hq = r.hk * greal + g;
-                p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
-            }
-        }
-        named_bar_sync(1, kConsumerWarps * 32);     // smem scratch reused by the next item
+        named_bar_sync(1, nthr);
+        finish_item(p, r, sM, sL, sO, sFin, sflag, sR, pitch, tid, nthr);
     }
 }
 
@@ -489,48 +1094,82 @@ static int num_sms() {
 static int round_group(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 
 struct AttnPlan {
-    int G, TPL, stages, nsplit, chunk;
+    bool mha12;                        // attn_mha12_kernel
+    bool polar;                        // attn_polar_kernel, else attn_lut_kernel
+    int G, TPL, stages, nsplit, chunk, tt, threads, smem, ctas_per_sm;
     bool tma;
-    SmemLayout L;
 };
+
+static bool tma_ok(const pkv_codec* c, const pkv_attn_args* a) {
+    const int row_bytes = (c->dim / 3) * a->code_bytes;
+    const uintptr_t kb = reinterpret_cast<uintptr_t>(a->k_codes), vb = reinterpret_cast<uintptr_t>(a->v_codes);
+    return (row_bytes % 16 == 0) && (kb % 16 == 0) && (vb % 16 == 0) &&
+           ((a->kv_batch_stride * a->code_bytes) % 16 == 0) && ((a->kv_head_stride * a->code_bytes) % 16 == 0);
+}
 
 static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     AttnPlan pl{};
     const int m = c->dim / 3;
-    const int g = a->q_heads / a->kv_heads;
-    pl.G = round_group(g);
-    pl.TPL = (m <= 32) ? 1 : 2;
-    const int row_bytes = m * a->code_bytes;
-    pl.stages = (row_bytes <= 64) ? 4 : 3;
+    pl.G = round_group(a->q_heads / a->kv_heads);
+    pl.tma = tma_ok(c, a);
     const int Cz = 1 << c->bits_z;
-    const int n_xy = (c->xy_per_z ? Cz : 1) << (c->bits_r + c->bits_theta);
-    pl.L = attn_smem_layout(m, a->code_bytes, c->dim, pl.G, n_xy, Cz, pl.stages);
-    while (pl.L.total > 227 * 1024 && pl.stages > 2) {      // large head dims: shallower ring
-        --pl.stages;
-        pl.L = attn_smem_layout(m, a->code_bytes, c->dim, pl.G, n_xy, Cz, pl.stages);
+    pl.polar = pl.tma && m <= 32 && c->xy_mode == 0 && c->bits_z <= 4 && (c->bits_r + c->bits_theta) <= 8 &&
+               (c->xy_per_z == 0 || c->bias_xy != nullptr);
+    pl.mha12 = pl.polar && c->dim == 96 && a->code_bytes == 2 && c->bits_z == 4 && c->bits_r == 4 &&
+               c->bits_theta == 4 && pl.G == 1 && a->q_heads == a->kv_heads && c->xy_per_z == 0 &&
+               (c->flags & PKV_CODEC_Z_UNIFORM) != 0;
+    if (pl.mha12) {
+        pl.TPL = 1;
+        pl.tt = mha12::TT;
+        pl.threads = mha12::W * 32 + 32;
+        pl.stages = mha12::STAGES;
+        pl.smem = mha12::TOTAL;
+        pl.chunk = mha12::CH;
+        pl.ctas_per_sm = 2;
+    } else if (pl.polar) {
+        pl.TPL = 1;
+        pl.tt = kPTT;
+        pl.threads = kPW * 32 + 32;
+        pl.stages = (m * a->code_bytes <= 32) ? 4 : 3;
+        PolarLayout L = polar_layout(m, a->code_bytes, c->dim, pl.G, c->bits_z, c->bits_r, c->bits_theta, pl.stages);
+        pl.smem = L.total;
+        pl.chunk = L.chunk;
+        pl.ctas_per_sm = 2;
+    } else {
+        pl.TPL = (m <= 32) ? 1 : 2;
+        pl.tt = kLTT;
+        pl.threads = pl.tma ? kLW * 32 + 32 : kLW * 32;
+        const int n_xy = (c->xy_per_z ? Cz : 1) << (c->bits_r + c->bits_theta);
+        pl.stages = (m * a->code_bytes <= 64) ? 4 : 3;
+        LutLayout L = lut_layout(m, a->code_bytes, c->dim, pl.G, n_xy, Cz, pl.stages);
+        while (L.total > 227 * 1024 && pl.stages > 2) {
+            --pl.stages;
+            L = lut_layout(m, a->code_bytes, c->dim, pl.G, n_xy, Cz, pl.stages);
+        }
+        pl.smem = L.total;
+        pl.chunk = 1 << 30;
+        pl.ctas_per_sm = 2;
     }
-    // TMA needs 16-byte aligned rows and bases
-    const uintptr_t kb = reinterpret_cast<uintptr_t>(a->k_codes), vb = reinterpret_cast<uintptr_t>(a->v_codes);
-    pl.tma = (row_bytes % 16 == 0) && (kb % 16 == 0) && (vb % 16 == 0) &&
-             ((a->kv_batch_stride * a->code_bytes) % 16 == 0) && ((a->kv_head_stride * a->code_bytes) % 16 == 0);
-    // split count: minimise rounds * (tiles per item + overhead)
-    const int tiles_total = std::max(1, (a->seq_len + kTT - 1) / kTT);
+    // split count: minimise rounds * (tiles per item + overhead); items carry at most `chunk` tokens
+    const int tiles_total = std::max(1, (a->seq_len + pl.tt - 1) / pl.tt);
+    const int max_tiles_item = std::max(1, pl.chunk / pl.tt);
     const int64_t units = (int64_t)a->batch * a->kv_heads;
-    const int64_t grid = (int64_t)num_sms() * 2;
-    int best = 1;
+    const int64_t grid = (int64_t)num_sms() * pl.ctas_per_sm;
+    int best = 0;
     double best_cost = 1e300;
-    int max_split = a->num_splits > 0 ? a->num_splits : std::min(tiles_total, 64);
-    int min_split = a->num_splits > 0 ? a->num_splits : 1;
-    for (int ns = min_split; ns <= max_split; ++ns) {
+    const int min_split = a->num_splits > 0 ? a->num_splits : (tiles_total + max_tiles_item - 1) / max_tiles_item;
+    const int max_split = a->num_splits > 0 ? a->num_splits : std::max(min_split, std::min(tiles_total, 64));
+    for (int ns = std::max(1, min_split); ns <= max_split; ++ns) {
         const int tiles_per = (tiles_total + ns - 1) / ns;
+        if (tiles_per > max_tiles_item) continue;
         const int64_t items = units * ns;
         const int64_t rounds = (items + grid - 1) / grid;
-        const double cost = (double)rounds * (tiles_per + 0.75) + (ns > 1 ? 0.25 : 0.0);
+        const double cost = (double)rounds * (tiles_per + 1.0) + (ns > 1 ? 0.25 : 0.0);
         if (cost < best_cost - 1e-9) { best_cost = cost; best = ns; }
     }
-    pl.chunk = ((tiles_total + best - 1) / best) * kTT;
-    pl.nsplit = (a->seq_len + pl.chunk - 1) / pl.chunk;
-    if (pl.nsplit < 1) pl.nsplit = 1;
+    if (best == 0) best = (tiles_total + max_tiles_item - 1) / max_tiles_item;
+    pl.chunk = ((tiles_total + best - 1) / best) * pl.tt;
+    pl.nsplit = std::max(1, (a->seq_len + pl.chunk - 1) / pl.chunk);
     return pl;
 }
 
@@ -542,45 +1181,61 @@ size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a) {
     return part + (size_t)a->batch * a->kv_heads * sizeof(int32_t);
 }
 
-template <int CB, int TPL, int G, bool TMA>
-static int launch_attn_t(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
-    auto kern = attn_decode_kernel<CB, TPL, G, TMA>;
-    const int threads = TMA ? 160 : 128;
-    const size_t smem = pl.L.total;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+template <typename K>
+static int launch_kernel(K kern, const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem) != cudaSuccess)
         return PKV_ERR_CUDA;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm <= 0)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, pl.threads, pl.smem) != cudaSuccess ||
+        per_sm <= 0)
         return PKV_ERR_CUDA;
     const int grid = (int)std::min<int64_t>(p.num_items, (int64_t)per_sm * num_sms());
-    kern<<<grid, threads, smem, st>>>(p);
+    kern<<<grid, pl.threads, pl.smem, st>>>(p);
     return cudaGetLastError() == cudaSuccess ? PKV_OK : PKV_ERR_CUDA;
 }
 
+template <int CB, int G>
+static int launch_polar_g(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
+    return p.bias_xy ? launch_kernel(attn_polar_kernel<CB, G, true>, p, pl, st)
+                     : launch_kernel(attn_polar_kernel<CB, G, false>, p, pl, st);
+}
+
+template <int CB>
+static int launch_polar(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
+    switch (pl.G) {
+        case 1: return launch_polar_g<CB, 1>(p, pl, st);
+        case 2: return launch_polar_g<CB, 2>(p, pl, st);
+        case 4: return launch_polar_g<CB, 4>(p, pl, st);
+        case 8: return launch_polar_g<CB, 8>(p, pl, st);
+    }
+    return PKV_ERR_UNSUPPORTED;
+}
+
 template <int CB, int TPL, int G>
-static int launch_attn_g(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
-    return pl.tma ? launch_attn_t<CB, TPL, G, true>(p, pl, st) : launch_attn_t<CB, TPL, G, false>(p, pl, st);
+static int launch_lut_g(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
+    return pl.tma ? launch_kernel(attn_lut_kernel<CB, TPL, G, true>, p, pl, st)
+                  : launch_kernel(attn_lut_kernel<CB, TPL, G, false>, p, pl, st);
 }
 
 template <int CB, int TPL>
-static int launch_attn_tpl(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
+static int launch_lut_tpl(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
     switch (pl.G) {
-        case 1: return launch_attn_g<CB, TPL, 1>(p, pl, st);
-        case 2: return launch_attn_g<CB, TPL, 2>(p, pl, st);
-        case 4: return launch_attn_g<CB, TPL, 4>(p, pl, st);
-        case 8: return launch_attn_g<CB, TPL, 8>(p, pl, st);
+        case 1: return launch_lut_g<CB, TPL, 1>(p, pl, st);
+        case 2: return launch_lut_g<CB, TPL, 2>(p, pl, st);
+        case 4: return launch_lut_g<CB, TPL, 4>(p, pl, st);
+        case 8: return launch_lut_g<CB, TPL, 8>(p, pl, st);
     }
     return PKV_ERR_UNSUPPORTED;
 }
 
 template <int CB>
-static int launch_attn_cb(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
-    return pl.TPL == 1 ? launch_attn_tpl<CB, 1>(p, pl, st) : launch_attn_tpl<CB, 2>(p, pl, st);
+static int launch_lut(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) {
+    return pl.TPL == 1 ? launch_lut_tpl<CB, 1>(p, pl, st) : launch_lut_tpl<CB, 2>(p, pl, st);
 }
 
 int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
     AttnPlan pl = plan_attn(c, a);
-    if (pl.L.total > 227 * 1024) return PKV_ERR_UNSUPPORTED;
+    if (pl.smem > 227 * 1024) return PKV_ERR_UNSUPPORTED;
     AttnParams p{};
     p.B = a->batch; p.Hq = a->q_heads; p.Hkv = a->kv_heads; p.S = a->seq_len;
     p.G = a->q_heads / a->kv_heads; p.m = c->dim / 3; p.dim = c->dim;
@@ -588,7 +1243,7 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
     p.kc = static_cast<const uint8_t*>(a->k_codes); p.vc = static_cast<const uint8_t*>(a->v_codes);
     p.kv_bs = a->kv_batch_stride; p.kv_hs = a->kv_head_stride;
     p.seq_lens = a->seq_lens;
-    p.scale_log2 = a->scale * 1.4426950408889634f;
+    p.scale_log2 = a->scale * kLog2e;
     p.out = a->out; p.out_bs = a->out_batch_stride; p.out_hs = a->out_head_stride;
     p.nsplit = pl.nsplit; p.chunk = pl.chunk;
     p.partial_only = a->partial_only; p.partial_out = a->partial_out;
@@ -600,17 +1255,21 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
         p.ws_part = static_cast<float*>(ws);
         p.ws_count = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + part);
     }
-    p.R = c->R; p.dec_z = c->dec_z; p.dec_xy = c->dec_xy;
+    p.R = c->R; p.dec_z = c->dec_z; p.dec_xy = c->dec_xy; p.bias_xy = c->bias_xy;
+    p.bits_z = c->bits_z; p.bits_r = c->bits_r; p.bits_t = c->bits_theta;
     p.bits_flat = c->bits_r + c->bits_theta;
     p.code_mask = (1 << (c->bits_z + p.bits_flat)) - 1;
     p.flat_mask = (1 << p.bits_flat) - 1;
     p.xy_per_z = c->xy_per_z;
     p.Cz = 1 << c->bits_z;
     p.n_xy = (c->xy_per_z ? p.Cz : 1) << p.bits_flat;
+    p.r_max = c->r_max;
     p.num_items = a->batch * a->kv_heads * pl.nsplit;
     p.stages = pl.stages;
     if (p.num_items == 0) return PKV_OK;
-    return a->code_bytes == 1 ? launch_attn_cb<1>(p, pl, st) : launch_attn_cb<2>(p, pl, st);
+    if (pl.mha12) return launch_kernel(attn_mha12_kernel, p, pl, st);
+    if (pl.polar) return a->code_bytes == 1 ? launch_polar<1>(p, pl, st) : launch_polar<2>(p, pl, st);
+    return a->code_bytes == 1 ? launch_lut<1>(p, pl, st) : launch_lut<2>(p, pl, st);
 }
 
 int launch_lse_combine(const pkv_codec* c, const float* parts, int n_parts, int64_t part_stride,

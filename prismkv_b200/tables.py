@@ -190,6 +190,7 @@ class HostTables:
     xy_per_z: int
     z_nan_bin: int
     z_hi: float
+    r_max: float
     R: np.ndarray
     z_thr: np.ndarray
     r2_thr: np.ndarray
@@ -197,6 +198,8 @@ class HostTables:
     codebook: np.ndarray
     dec_z: np.ndarray
     dec_xy: np.ndarray
+    bias_xy: Optional[np.ndarray] = None     # (C_z, 2) clamped BiasTable (x, y) terms
+    z_uniform: bool = False                  # dec_z[i] = z_min + (i + 0.5) * delta_z (no Lloyd-Max, no bias)
 
 
 def build_host_tables(dim: int, bits_z: int, bits_r: int, bits_theta: int, R: np.ndarray,
@@ -227,15 +230,18 @@ def build_host_tables(dim: int, bits_z: int, bits_r: int, bits_theta: int, R: np
         xy = np.broadcast_to(dec_xy_polar(r_max, bits_r, bits_theta), (Cz, K, 2)).copy()
         xy_mode = 0
     xy_per_z = int(codebook is not None or bias_table is not None)
+    bias_xy = None
     if bias_table is not None:
         clip = F32(bias_delta_z / 2.0)
         b = np.clip(np.asarray(bias_table, dtype=F32), -clip, clip).astype(F32)   # (Cz, 3)
         dz = (dz - b[:, 0]).astype(F32)
         xy = (xy - b[:, None, 1:3]).astype(F32)
+        bias_xy = np.ascontiguousarray(b[:, 1:3])
     if not xy_per_z:
         xy = xy[0]
     return HostTables(dim=dim, bits=(bits_z, bits_r, bits_theta), xy_mode=xy_mode, xy_per_z=xy_per_z,
-                      z_nan_bin=z_nan_bin, z_hi=float(z_hi),
+                      z_nan_bin=z_nan_bin, z_hi=float(z_hi), r_max=float(r_max),
                       R=np.ascontiguousarray(R, dtype=F32), z_thr=z_thr.astype(F32),
                       r2_thr=r2.astype(F32), th_thr=th.astype(F32), codebook=cb,
-                      dec_z=dz.astype(F32), dec_xy=np.ascontiguousarray(xy, dtype=F32))
+                      dec_z=dz.astype(F32), dec_xy=np.ascontiguousarray(xy, dtype=F32), bias_xy=bias_xy,
+                      z_uniform=(lloyd_boundaries is None and lloyd_centroids is None and bias_table is None))

@@ -110,7 +110,7 @@ def test_encode_half_inputs(cuda_ready, dtype):
 
 @pytest.mark.parametrize("variant,bits", [("v1", (4, 4, 4)), ("learned_bias", (4, 4, 4)),
                                           ("lloyd", (4, 4, 4)), ("v1", (3, 3, 2))], ids=str)
-@pytest.mark.parametrize("out_dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 6e-2), (torch.float16, 8e-3)])
+@pytest.mark.parametrize("out_dtype,tol", [(torch.float32, 0.0), (torch.bfloat16, 2.0 ** -8), (torch.float16, 2.0 ** -11)])
 def test_decode_matches_oracle(cuda_ready, variant, bits, out_dtype, tol):
     q = _quantizer(variant, bits)
     p = _params(q)
@@ -118,8 +118,8 @@ def test_decode_matches_oracle(cuda_ready, variant, bits, out_dtype, tol):
     codes = torch.randint(0, 1 << sum(bits), (30011, 32), generator=g)
     ref = oracle.decode(codes.numpy(), q.R.numpy(), p)
     out = q.codec(torch.device(DEV)).decode(codes.to(DEV), out_dtype=out_dtype).float().cpu().numpy()
-    # bf16/fp16 outputs: relative rounding of |v| <= ~10
-    np.testing.assert_allclose(out, ref, atol=tol, rtol=0)
+    # fp32: GEMM rounding; bf16/fp16: one rounding of the fp32 result (half an ulp, relative)
+    np.testing.assert_allclose(out, ref, atol=1e-5, rtol=tol)
 
 
 @pytest.mark.parametrize("n", [0, 1, 63, 64, 65, 127, 128, 129, 4097])
@@ -173,8 +173,11 @@ def test_reencode_of_decoded_is_idempotent_full_size(cuda_ready, variant):
     c1 = q.encode(X)
     c2 = q.encode(q.decode(c1))
     if variant == "v1":
+        # angle bins 0 and 15 are the same direction (theta = -pi and +pi are both grid
+        # points, stacked_plane.py:255,307): a decoded -pi may come back as +pi
         ir = (c1 >> 4) & 15
+        fold = lambda c: torch.where((c & 15) == 15, c - 15, c)
         keep = ir != 0
-        assert torch.equal(c1[keep], c2[keep])
+        assert torch.equal(fold(c1[keep]), fold(c2[keep]))
     else:
         assert (c1 != c2).float().mean().item() < 1e-4      # duplicate-nearest centroids only
