@@ -113,39 +113,41 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
 }
 
 // rotated, scaled query of every head of the group -> sQ[G][dim]:
-// sQ[g][k] = scale*log2(e) * sum_i q[g][i] R[k][i].  One warp per output row k,
-// lanes over i (coalesced rows of R), shuffle reduction.
+// sQ[g][k] = scale*log2(e) * sum_i q[g][i] R[k][i].  The raw query is staged in
+// shared memory (sQraw, G*dim floats); one thread per output row k issues all
+// loads of row k before the multiply-adds, so a rotation costs one memory
+// round trip.  Rp: R with row pitch `pitch` (global or shared).
 template <int G>
 __device__ __forceinline__ void rotate_query(const AttnParams& p, const ItemRange& r, const float* Rp, int pitch,
-                                             float* sQ, int tid, int nthr) {
-    const int dim = p.dim, lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
-    float qv[G][6];                                   // dim <= 192: six per lane
-    #pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const int hq = r.hk * p.G + g;
-        const int64_t qb = (int64_t)r.b * p.q_bs + (int64_t)hq * p.q_hs;
-        #pragma unroll
-        for (int u = 0; u < 6; ++u) {
-            const int i = lane + 32 * u;
-            qv[g][u] = (g < p.G && i < dim) ? q_load(p.q, p.qdt, qb + i) : 0.f;
+                                             float* sQ, float* sQraw, int tid, int nthr) {
+    const int dim = p.dim;
+    for (int idx = tid; idx < G * dim; idx += nthr) {
+        const int g = idx / dim, i = idx % dim;
+        float v = 0.f;
+        if (g < p.G) {
+            const int hq = r.hk * p.G + g;
+            v = q_load(p.q, p.qdt, (int64_t)r.b * p.q_bs + (int64_t)hq * p.q_hs + i);
         }
+        sQraw[idx] = v;
     }
-    for (int k = warp; k < dim; k += nw) {
-        float rv[6];
+    named_bar_sync(1, nthr);
+    for (int k = tid; k < dim; k += nthr) {
+        const float* row = Rp + k * pitch;
+        float acc[G];
         #pragma unroll
-        for (int u = 0; u < 6; ++u) {
-            const int i = lane + 32 * u;
-            rv[u] = (i < dim) ? Rp[k * pitch + i] : 0.f;
+        for (int g = 0; g < G; ++g) acc[g] = 0.f;
+        for (int i0 = 0; i0 < dim; i0 += 32) {
+            float rv[32];
+            #pragma unroll
+            for (int u = 0; u < 32; ++u) rv[u] = (i0 + u < dim) ? row[i0 + u] : 0.f;
+            #pragma unroll
+            for (int g = 0; g < G; ++g)
+                #pragma unroll
+                for (int u = 0; u < 32; ++u)
+                    if (i0 + u < dim) acc[g] = fmaf(sQraw[g * dim + i0 + u], rv[u], acc[g]);
         }
         #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            float acc = 0.f;
-            #pragma unroll
-            for (int u = 0; u < 6; ++u) acc = fmaf(qv[g][u], rv[u], acc);
-            #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-            if (lane == 0) sQ[g * dim + k] = acc * p.scale_log2;
-        }
+        for (int g = 0; g < G; ++g) sQ[g * dim + k] = acc[g] * p.scale_log2;
     }
 }
 
@@ -216,8 +218,14 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
         for (int idx = tid; idx < greal * dim; idx += nthr) {
             const int g = idx / dim, i = idx % dim;
             float v = 0.f;
-            #pragma unroll 4
-            for (int k = 0; k < dim; ++k) v = fmaf(sFin[g * dim + k], Rp[k * pitch + i], v);
+            for (int k0 = 0; k0 < dim; k0 += 16) {
+                float rv[16];
+                #pragma unroll
+                for (int u = 0; u < 16; ++u) rv[u] = (k0 + u < dim) ? Rp[(k0 + u) * pitch + i] : 0.f;
+                #pragma unroll
+                for (int u = 0; u < 16; ++u)
+                    if (k0 + u < dim) v = fmaf(sFin[g * dim + k0 + u], rv[u], v);
+            }
             const int hq = r.hk * greal + g;
             p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
         }
@@ -366,7 +374,7 @@ __global__ void __launch_bounds__(kPW * 32 + 32, 2) attn_polar_kernel(AttnParams
         const ItemRange r = item_range(p, item);
         const int ntok = r.tok1 - r.tok0;
         const int ntiles = (ntok + kPTT - 1) / kPTT;
-        rotate_query<G>(p, r, p.R, dim, sQ, tid, nthr);
+        rotate_query<G>(p, r, p.R, dim, sQ, sFin, tid, nthr);
         named_bar_sync(1, nthr);
         // ---- query tables: one column per lane (bank = lane) ----------------
         if (G == 1) {
@@ -547,17 +555,20 @@ constexpr int TT = 256;                                // tokens per tile (32 pe
 constexpr int CH = 4096;                               // tokens per item (scores in smem)
 constexpr int STAGES = 3;
 constexpr int TILE = TT * 64;                          // 32 codes x 2 bytes per token
-constexpr int OFF_KT = STAGES * TILE;                  // [256][32] floats
-constexpr int OFF_CS = OFF_KT + 256 * 32 * 4;          // [16] float2
-constexpr int OFF_Q = OFF_CS + 16 * 8;                 // [96]
-constexpr int OFF_S = OFF_Q + 96 * 4 + 128;            // [CH]
+constexpr int RBYTES = 96 * 96 * 4;                    // the rotation, fp32, row pitch 96
+constexpr int OFF_RT = STAGES * TILE;                  // R, or the [256][32] score table
+constexpr int OFF_CS = OFF_RT + RBYTES;                // [16] float2
+constexpr int OFF_Q = OFF_CS + 16 * 8;                 // [96] rotated query
+constexpr int OFF_QRAW = OFF_Q + 96 * 4;               // [96] raw query
+constexpr int OFF_S = OFF_QRAW + 96 * 4;               // [CH]
 constexpr int OFF_RED = OFF_S + CH * 4;                // [2][W]
 constexpr int OFF_ACC = OFF_RED + 2 * W * 4;           // [W][96]
 constexpr int OFF_FIN = OFF_ACC + W * 96 * 4;          // [96]
 constexpr int OFF_MISC = OFF_FIN + 96 * 4;             // sM, sL, C, flag
-constexpr int OFF_BAR = OFF_MISC + 64;
-constexpr int TOTAL = OFF_BAR + 2 * STAGES * 8;
+constexpr int OFF_BAR = OFF_MISC + 64;                 // full[STAGES], empty[STAGES], rbar
+constexpr int TOTAL = OFF_BAR + (2 * STAGES + 1) * 8;
 constexpr float MAGIC = 8388608.f;                     // 2^23
+static_assert(256 * 32 * 4 <= RBYTES, "score table must fit the R region");
 }  // namespace mha12
 
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
@@ -569,6 +580,29 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
         "mov.b64 {%0, %1}, rd;\n\t}"
         : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
     return d;
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ float2 lds_f32x2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+    return v;
 }
 
 // 16-lane transpose-reduce within each half-warp: on exit v[0] of lane l holds
@@ -590,9 +624,11 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
     using namespace mha12;
     extern __shared__ __align__(128) uint8_t mha12_smem[];
     uint8_t* smem = mha12_smem;
-    float* kT = reinterpret_cast<float*>(smem + OFF_KT);
+    float* kT = reinterpret_cast<float*>(smem + OFF_RT);       // score table, or R between uses
+    const float* sR = kT;
     float2* vCS = reinterpret_cast<float2*>(smem + OFF_CS);
     float* sQ = reinterpret_cast<float*>(smem + OFF_Q);
+    float* sQraw = reinterpret_cast<float*>(smem + OFF_QRAW);
     float* sS = reinterpret_cast<float*>(smem + OFF_S);
     float* sRed = reinterpret_cast<float*>(smem + OFF_RED);
     float* sAcc = reinterpret_cast<float*>(smem + OFF_ACC);
@@ -603,6 +639,7 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
     int* sflag = reinterpret_cast<int*>(sM + 3);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + STAGES;
+    uint64_t* rbar = empty + STAGES;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const float dr = p.r_max / 15.f;
@@ -618,7 +655,17 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], W);
         }
+        mbar_init(rbar, 1);
         fence_mbar_init();
+        // R for the first item's query rotation, ahead of the code stream
+        mbar_arrive_expect_tx(rbar, RBYTES);
+        bulk_g2s(kT, p.R, RBYTES, rbar);
+    }
+    // the first item's query, ahead of the code stream too
+    float qreg = 0.f;
+    if (blockIdx.x < p.num_items && tid < 96) {
+        const ItemRange r = item_range(p, blockIdx.x);
+        qreg = q_load(p.q, p.qdt, (int64_t)r.b * p.q_bs + (int64_t)r.hk * p.q_hs + tid);
     }
     __syncthreads();
     if (warp == W) {
@@ -631,21 +678,41 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
     const int sh1 = half << 4, sh2 = 16 - sh1;          // which code of the word comes first
     const int wcol1 = lane, wcol2 = lane ^ 16;           // table words of the first / second code
     const int tg = lane >> 2, q4 = lane & 3;             // V: token-in-8, 8-triplet chunk
-    int seq = 0;
+    int seq = 0, ruse = 0;
     bool alive = true;
     for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
         const ItemRange r = item_range(p, item);
         const int ntok = r.tok1 - r.tok0;
         const int ntiles = (ntok + TT - 1) / TT;
-        rotate_query<1>(p, r, p.R, 96, sQ, tid, nthr);
+        if (tid < 96) sQraw[tid] = qreg;
+        if (alive && !mbar_wait(rbar, ruse & 1, kErrWaitFull)) alive = false;   // R in place
         named_bar_sync(1, nthr);
-        // score table: row e = (i_r << 4) | i_theta; word w < 16 -> triplet 2w, w >= 16 -> 2(w-16)+1
-        for (int idx = tid; idx < 256 * 32; idx += nthr) {
-            const int e = idx >> 5, w = idx & 31;
+        // q' = scale log2(e) R q: one warp per row, lanes over the input index
+        {
+            const float qa = sQraw[lane], qb = sQraw[lane + 32], qc = sQraw[lane + 64];
+            #pragma unroll 4
+            for (int k = warp; k < 96; k += W) {
+                const float* row = sR + k * 96;
+                float acc = fmaf(qa, row[lane], fmaf(qb, row[lane + 32], qc * row[lane + 64]));
+                #pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+                if (lane == 0) sQ[k] = acc * p.scale_log2;
+            }
+        }
+        named_bar_sync(1, nthr);
+        // score table over the R region: row e = (i_r << 4) | i_theta; word w < 16 -> triplet 2w,
+        // w >= 16 -> 2(w-16)+1.  Thread t fills column t & 31, rows (t >> 5) + 8k.
+        {
+            const int w = tid & 31, e0 = tid >> 5;
             const int j = (w < 16) ? 2 * w : 2 * (w - 16) + 1;
-            const float2 cs = vCS[e & 15];
-            const float fr = (float)(e & 0xF0);
-            kT[idx] = fr * (sQ[3 * j + 1] * cs.x + sQ[3 * j + 2] * cs.y);
+            const float qx = sQ[3 * j + 1], qy = sQ[3 * j + 2];
+            const float2 cs0 = vCS[e0 & 15], cs1 = vCS[(e0 + 8) & 15];
+            const float A0 = qx * cs0.x + qy * cs0.y, A1 = qx * cs1.x + qy * cs1.y;
+            #pragma unroll 8
+            for (int k = 0; k < 32; ++k) {
+                const int e = e0 + 8 * k;
+                kT[e * 32 + w] = (float)(e & 0xF0) * ((k & 1) ? A1 : A0);
+            }
         }
         if (warp == 0) {                                   // C = z0 * sum_j q'_z,j
             float c = sQ[3 * lane];
@@ -658,6 +725,8 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
         const int j1 = 2 * l16 + half, j2 = 2 * l16 + 1 - half;
         const float2 az = make_float2(sQ[3 * j1] * dz * (1.f / 256.f), sQ[3 * j2] * dz * (1.f / 256.f));
         const float C = sC[0];
+        const uint32_t kb1 = (uint32_t)__cvta_generic_to_shared(kT) + 4u * wcol1;   // this lane's table words
+        const uint32_t kb2 = (uint32_t)__cvta_generic_to_shared(kT) + 4u * wcol2;
 
         // ---- pass 1: K -> scores ------------------------------------------------
         float mx = -INFINITY;
@@ -675,8 +744,8 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
                     const float2 zz = fadd2(make_float2(__int_as_float((c1 & 0xF00u) | 0x4B000000u),
                                                         __int_as_float((c2 & 0xF00u) | 0x4B000000u)),
                                             make_float2(-MAGIC, -MAGIC));
-                    const float t1 = kT[((c1 & 0xFFu) << 5) + wcol1];
-                    const float t2 = kT[((c2 & 0xFFu) << 5) + wcol2];
+                    const float t1 = lds_f32(kb1 + (c1 & 0xFFu) * 128u);
+                    const float t2 = lds_f32(kb2 + (c2 & 0xFFu) * 128u);
                     const float2 a = ffma2(az, zz, make_float2(t1, t2));
                     ps[st] = a.x + a.y;
                 }
@@ -695,6 +764,21 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
         for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         if (lane == 0) sRed[warp] = mx;
         named_bar_sync(1, nthr);
+        // the score table is dead: bring R back for the finish and the next rotation
+        if (tid == 0) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(rbar, RBYTES);
+            bulk_g2s(kT, p.R, RBYTES, rbar);
+        }
+        ++ruse;
+        // prefetch the next item's query
+        {
+            const int nitem = item + gridDim.x;
+            if (nitem < p.num_items && tid < 96) {
+                const ItemRange rn = item_range(p, nitem);
+                qreg = q_load(p.q, p.qdt, (int64_t)rn.b * p.q_bs + (int64_t)rn.hk * p.q_hs + tid);
+            }
+        }
         float M = -INFINITY;
         #pragma unroll
         for (int w = 0; w < W; ++w) M = fmaxf(M, sRed[w]);
@@ -745,15 +829,12 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
                         const float2 rf = fadd2(make_float2(__int_as_float((w & 0xF0u) | 0x4B000000u),
                                                             __int_as_float(((w >> 16) & 0xF0u) | 0x4B000000u)),
                                                 make_float2(-MAGIC, -MAGIC));
-                        float2 cs0, cs1;
-                        asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(cs0.x), "=f"(cs0.y)
-                                     : "r"(csb + ((w << 3) & 0x78u)));
-                        asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(cs1.x), "=f"(cs1.y)
-                                     : "r"(csb + ((w >> 13) & 0x78u)));
+                        const float2 cs0 = lds_f32x2(csb | ((w << 3) & 0x78u));      // table is 128-byte aligned
+                        const float2 cs1 = lds_f32x2(csb | ((w >> 13) & 0x78u));
                         azz[h] = ffma2(make_float2(pw, pw), zf, azz[h]);
-                        const float w0 = pw * rf.x, w1 = pw * rf.y;
-                        axy[2 * h] = ffma2(make_float2(w0, w0), cs0, axy[2 * h]);
-                        axy[2 * h + 1] = ffma2(make_float2(w1, w1), cs1, axy[2 * h + 1]);
+                        const float2 wr = fmul2(make_float2(pw, pw), rf);
+                        axy[2 * h] = ffma2(make_float2(wr.x, wr.x), cs0, axy[2 * h]);
+                        axy[2 * h + 1] = ffma2(make_float2(wr.y, wr.y), cs1, axy[2 * h + 1]);
                     }
                 }
             }
@@ -791,9 +872,12 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
             if (tid % 3 == 0) v = fmaf(z0, sL[0], v * dz * (1.f / 256.f));
             sAcc[tid] = v;
         }
+        if (alive && !mbar_wait(rbar, ruse & 1, kErrWaitFull)) alive = false;   // R back in place
         named_bar_sync(1, nthr);
-        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, 96, tid, nthr);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr);
     }
+    // the last R copy must land before the CTA exits
+    if (tid == 0 && alive) mbar_wait(rbar, ruse & 1, kErrWaitDrain);
 }
 
 // ===========================================================================
@@ -885,7 +969,7 @@ __global__ void __launch_bounds__(TMA ? kLW * 32 + 32 : kLW * 32) attn_lut_kerne
     for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
         const ItemRange r = item_range(p, item);
         const int greal = p.G;
-        rotate_query<G>(p, r, sR, pitch, sQ, tid, nthr);
+        rotate_query<G>(p, r, sR, pitch, sQ, sFin, tid, nthr);
         named_bar_sync(1, nthr);
         float qv[G][TPL][3];
         #pragma unroll

@@ -96,26 +96,29 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    // suspends the thread in hardware until the phase completes or ~20 us pass
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(20000u) : "memory");
     return ok != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete; gives up after ~`limit`
-// polls (each try_wait itself blocks for a hardware-defined interval), sets
-// the device error word and returns false.
+// Wait for phase `parity` of `bar` to complete.  Gives up after `limit`
+// suspended polls (about 20 us each, so ~2.6 s by default), sets the device
+// error word and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_t err,
-                                          uint32_t limit = (1u << 22)) {
-    for (uint32_t i = 0; i < limit; ++i) {
+                                          uint32_t limit = (1u << 17)) {
+    for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
-        if (i > 64) __nanosleep(64);
-    }
     flag_error(err);
     return false;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
