@@ -675,7 +675,6 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
 
     constexpr int nthr = W * 32;
     const int half = lane >> 4, l16 = lane & 15;
-    const int sh1 = half << 4, sh2 = 16 - sh1;          // which code of the word comes first
     const int wcol1 = lane, wcol2 = lane ^ 16;           // table words of the first / second code
     const int tg = lane >> 2, q4 = lane & 3;             // V: token-in-8, 8-triplet chunk
     int seq = 0, ruse = 0;
@@ -727,6 +726,11 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
         const float C = sC[0];
         const uint32_t kb1 = (uint32_t)__cvta_generic_to_shared(kT) + 4u * wcol1;   // this lane's table words
         const uint32_t kb2 = (uint32_t)__cvta_generic_to_shared(kT) + 4u * wcol2;
+        // byte selectors: a word holds two 12-bit codes, the first in bytes 0-1.  selr* pull the
+        // low byte (the flat polar index); selz* put byte 1 (z in its low nibble) under the
+        // 2^23 exponent, giving 2^23 + 256 i_z.  Half 1 of the warp takes the codes swapped.
+        const uint32_t selr1 = half ? 0x4442u : 0x4440u, selr2 = half ? 0x4440u : 0x4442u;
+        const uint32_t selz1 = half ? 0x7534u : 0x7514u, selz2 = half ? 0x7514u : 0x7534u;
 
         // ---- pass 1: K -> scores ------------------------------------------------
         float mx = -INFINITY;
@@ -740,12 +744,12 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
                 #pragma unroll
                 for (int st = 0; st < 16; ++st) {
                     const uint32_t w = K32[(warp * 32 + 2 * st + half) * 16 + l16];
-                    const uint32_t c1 = w >> sh1, c2 = w >> sh2;
-                    const float2 zz = fadd2(make_float2(__int_as_float((c1 & 0xF00u) | 0x4B000000u),
-                                                        __int_as_float((c2 & 0xF00u) | 0x4B000000u)),
+                    const uint32_t i1 = __byte_perm(w, 0u, selr1), i2 = __byte_perm(w, 0u, selr2);
+                    const float2 zz = fadd2(make_float2(__int_as_float(__byte_perm(w, 0x4B000000u, selz1)),
+                                                        __int_as_float(__byte_perm(w, 0x4B000000u, selz2))),
                                             make_float2(-MAGIC, -MAGIC));
-                    const float t1 = lds_f32(kb1 + (c1 & 0xFFu) * 128u);
-                    const float t2 = lds_f32(kb2 + (c2 & 0xFFu) * 128u);
+                    const float t1 = lds_f32(kb1 + i1 * 128u);
+                    const float t2 = lds_f32(kb2 + i2 * 128u);
                     const float2 a = ffma2(az, zz, make_float2(t1, t2));
                     ps[st] = a.x + a.y;
                 }
