@@ -210,6 +210,11 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
                     sFin[g * dim + (k - 2)] = (lsw > 0.f) ? v / lsw : 0.f;
                 }
             }
+            // Clear the consumed partials: a workspace shared by calls of other shapes puts its
+            // counters at other offsets, so every byte must be zero again after each call.
+            named_bar_sync(1, nthr);
+            float* rows = p.ws_part + ((int64_t)r.b * p.Hq + (int64_t)r.hk * greal) * p.nsplit * (dim + 2);
+            for (int idx = tid; idx < greal * p.nsplit * (dim + 2); idx += nthr) rows[idx] = 0.f;
             finalize = !p.partial_only;
         }
     }

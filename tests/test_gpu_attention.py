@@ -180,6 +180,24 @@ def test_attention_repeated_calls_reuse_workspace(cuda_ready):
     assert _lib.device_error() == 0
 
 
+def test_attention_shapes_in_turn_share_workspace(cuda_ready):
+    """Calls of different shapes through one per-stream workspace: the arrival
+    counters of each shape sit at a different offset, so every call must leave
+    the whole workspace (partials included) zeroed for the next one."""
+    q, p = _setup("v1", (4, 4, 4))
+    cases = [(4, 8, 20000, 0), (1, 2, 5000, 5), (3, 4, 7000, 4), (4, 8, 20000, 0)]
+    data = []
+    for i, (B, H, S, ns) in enumerate(cases):
+        kc, vc = _codes(q, B, H, S, seed=20 + i % 3)
+        qv = torch.randn(B, H, 96, generator=torch.Generator(device=DEV).manual_seed(i % 3), device=DEV)
+        data.append((qv, kc, vc, ns))
+    for qv, kc, vc, ns in data:
+        out = decode_attention(q, qv, kc, vc, num_splits=ns)
+        ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64),
+                               vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
+        np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+
+
 def test_phi3_decode_full_size(cuda_ready):
     """The benchmark workload at full size (B=8, 32 heads, S=4096) against the oracle."""
     from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
