@@ -51,7 +51,9 @@ enum {
     PKV_ERR_ALIGNMENT = 3,    /* pointer or stride misaligned for the call       */
     PKV_ERR_WORKSPACE = 4,    /* workspace missing or smaller than required      */
     PKV_ERR_CUDA = 5,         /* CUDA runtime reported an error (launch/config)  */
-    PKV_ERR_DEVICE = 6        /* a kernel flagged an error (bounded wait expired)*/
+    PKV_ERR_DEVICE = 6,       /* a kernel flagged an error (bounded wait expired)*/
+    PKV_ERR_SCRATCH_LIMIT = 7 /* pkv_attn_decode_noalloc: needs more scratch than
+                                 its static array holds                          */
 };
 
 /* ---- codec flags -------------------------------------------------------- */
@@ -149,6 +151,24 @@ PKV_API size_t pkv_attn_workspace_size(const pkv_codec *c, const pkv_attn_args *
 PKV_API int pkv_workspace_init(void *workspace, size_t bytes, void *stream);
 PKV_API int pkv_attn_decode(const pkv_codec *c, const pkv_attn_args *a,
                     void *workspace, size_t workspace_bytes, void *stream);
+
+/* pkv_attn_decode without a caller workspace: the split partials and arrival
+ * counters live in one static device array of PKV_NOALLOC_SCRATCH_BYTES
+ * (8 MiB) per device, for callers that cannot allocate device memory on the
+ * decode path (a C/C++ host without a caching allocator, where cudaMalloc
+ * would synchronise the device every step).  It has no counterpart in the
+ * reference.  Limits: the partials, batch * q_heads * splits * (dim + 2)
+ * floats rounded up to 256 bytes, must fit in 8 MiB - 64 KiB, and
+ * batch * kv_heads must not exceed PKV_NOALLOC_MAX_KV_ROWS when the call
+ * splits; otherwise PKV_ERR_SCRATCH_LIMIT and nothing is launched.  The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress, with
+ * that device current) and zeroes its counter region on `stream`; make it
+ * before any stream capture.  The counters must be zero when a kernel starts;
+ * each call leaves them zero.  The array is shared: calls that overlap in
+ * time on one device (other streams, unsynchronised threads) race on it.   */
+#define PKV_NOALLOC_SCRATCH_BYTES (8u << 20)
+#define PKV_NOALLOC_MAX_KV_ROWS 16384
+PKV_API int pkv_attn_decode_noalloc(const pkv_codec *c, const pkv_attn_args *a, void *stream);
 
 /* Merge n_parts partials per row (row r of part p at
  * partials + p*part_stride + r*(dim+2)), normalise, rotate back with R and

@@ -23,7 +23,7 @@ DTYPE_CODES = {torch.float32: PKV_F32, torch.bfloat16: PKV_BF16, torch.float16: 
 
 EXPORTED = ("pkv_abi_version", "pkv_strerror", "pkv_device_error", "pkv_encode", "pkv_decode",
             "pkv_attn_workspace_size", "pkv_workspace_init", "pkv_attn_decode", "pkv_lse_combine",
-            "pkv_polar_scores")
+            "pkv_polar_scores", "pkv_attn_decode_noalloc")
 
 
 class PkvCodec(ctypes.Structure):
@@ -67,6 +67,8 @@ def _declare(lib):
     lib.pkv_workspace_init.argtypes = [c_void_p, c_size_t, c_void_p]
     lib.pkv_attn_decode.restype = c_int32
     lib.pkv_attn_decode.argtypes = [P(PkvCodec), P(PkvAttnArgs), c_void_p, c_size_t, c_void_p]
+    lib.pkv_attn_decode_noalloc.restype = c_int32
+    lib.pkv_attn_decode_noalloc.argtypes = [P(PkvCodec), P(PkvAttnArgs), c_void_p]
     lib.pkv_lse_combine.restype = c_int32
     lib.pkv_lse_combine.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int32, c_void_p, c_int64, c_void_p]
     lib.pkv_polar_scores.restype = c_int32

@@ -67,6 +67,9 @@ const char* pkv_strerror(int status) {
         case PKV_ERR_WORKSPACE: return "workspace missing or too small";
         case PKV_ERR_CUDA: return "CUDA runtime error";
         case PKV_ERR_DEVICE: return "device-side error flag set (a bounded wait expired)";
+        case PKV_ERR_SCRATCH_LIMIT:
+            return "arguments need more split scratch than the static array of pkv_attn_decode_noalloc holds "
+                   "(8 MiB - 64 KiB of partials, 16384 batch x kv-head rows); use pkv_attn_decode with a workspace";
     }
     return "unknown status";
 }

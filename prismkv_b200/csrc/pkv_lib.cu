@@ -4,3 +4,4 @@
 #include "pkv_attn.cu"
 #include "pkv_scores.cu"
 #include "pkv_api.cu"
+#include "pkv_noalloc.cu"

@@ -33,7 +33,7 @@ def test_abi_version_and_strerror():
     lib = _lib.load()
     assert lib.pkv_abi_version() == 1
     assert lib.pkv_strerror(0) == b"ok"
-    for code in range(1, 7):
+    for code in range(1, 8):
         assert lib.pkv_strerror(code) and lib.pkv_strerror(code) != b"unknown status"
     assert lib.pkv_strerror(99) == b"unknown status"
 
