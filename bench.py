@@ -202,6 +202,8 @@ def bench_decode(args, ws, rank, device):
     scrub = L2Scrub(device)
     stream = torch.cuda.current_stream(device)
 
+    plan = codec.describe(q, kc, vc)
+
     def step():
         codec.attention(q, kc, vc, out=out)
 
@@ -278,8 +280,8 @@ def bench_decode(args, ws, rank, device):
                    "parallelism": f"replicas x{ws}"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": _committed_traffic("attn_decode_kernel", w.name),
-                     "kernel": "pkv::attn_decode_kernel"},
+                     "traffic": _committed_traffic(plan["kernel"], w.name),
+                     "kernel": plan["kernel"], "num_splits": plan["num_splits"]},
         "e2e": {"value": round(nbytes * ws / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": args.steps,
@@ -391,7 +393,7 @@ def bench_reference(args, ws, rank):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="prismkv", choices=["prismkv", "reference"])
     ap.add_argument("--workload", default="phi3-decode")

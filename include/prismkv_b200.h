@@ -152,6 +152,20 @@ PKV_API int pkv_workspace_init(void *workspace, size_t bytes, void *stream);
 PKV_API int pkv_attn_decode(const pkv_codec *c, const pkv_attn_args *a,
                     void *workspace, size_t workspace_bytes, void *stream);
 
+/* Which kernel and split plan pkv_attn_decode would use for these arguments
+ * (introspection for tests and benchmarks; launches nothing; the output
+ * pointers of `a` may be null).                                           */
+enum { PKV_KERNEL_MHA12 = 1, PKV_KERNEL_POLAR = 2, PKV_KERNEL_LUT = 3 };
+typedef struct pkv_attn_plan {
+    int32_t kernel;            /* PKV_KERNEL_*                                  */
+    int32_t num_splits;        /* sequence splits per (batch, kv head)          */
+    int32_t tokens_per_split;
+    int32_t threads;           /* per CTA                                       */
+    int32_t smem_bytes;        /* dynamic shared memory per CTA                 */
+    int32_t ctas_per_sm;       /* residency the schedule is planned for         */
+} pkv_attn_plan;
+PKV_API int pkv_attn_describe(const pkv_codec *c, const pkv_attn_args *a, pkv_attn_plan *out);
+
 /* pkv_attn_decode without a caller workspace: the split partials and arrival
  * counters live in one static device array of PKV_NOALLOC_SCRATCH_BYTES
  * (8 MiB) per device, for callers that cannot allocate device memory on the

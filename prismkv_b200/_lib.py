@@ -23,7 +23,7 @@ DTYPE_CODES = {torch.float32: PKV_F32, torch.bfloat16: PKV_BF16, torch.float16: 
 
 EXPORTED = ("pkv_abi_version", "pkv_strerror", "pkv_device_error", "pkv_encode", "pkv_decode",
             "pkv_attn_workspace_size", "pkv_workspace_init", "pkv_attn_decode", "pkv_lse_combine",
-            "pkv_polar_scores", "pkv_attn_decode_noalloc")
+            "pkv_polar_scores", "pkv_attn_decode_noalloc", "pkv_attn_describe")
 
 
 class PkvCodec(ctypes.Structure):
@@ -44,6 +44,13 @@ class PkvAttnArgs(ctypes.Structure):
                 ("out", c_void_p), ("out_batch_stride", c_int64), ("out_head_stride", c_int64),
                 ("num_splits", c_int32), ("partial_only", c_int32), ("partial_out", c_void_p)]
 
+
+class PkvAttnPlan(ctypes.Structure):
+    _fields_ = [("kernel", c_int32), ("num_splits", c_int32), ("tokens_per_split", c_int32),
+                ("threads", c_int32), ("smem_bytes", c_int32), ("ctas_per_sm", c_int32)]
+
+
+KERNEL_NAMES = {1: "attn_mha12_kernel", 2: "attn_polar_kernel", 3: "attn_lut_kernel"}
 
 _lock = threading.Lock()
 _lib = None
@@ -69,6 +76,8 @@ def _declare(lib):
     lib.pkv_attn_decode.argtypes = [P(PkvCodec), P(PkvAttnArgs), c_void_p, c_size_t, c_void_p]
     lib.pkv_attn_decode_noalloc.restype = c_int32
     lib.pkv_attn_decode_noalloc.argtypes = [P(PkvCodec), P(PkvAttnArgs), c_void_p]
+    lib.pkv_attn_describe.restype = c_int32
+    lib.pkv_attn_describe.argtypes = [P(PkvCodec), P(PkvAttnArgs), P(PkvAttnPlan)]
     lib.pkv_lse_combine.restype = c_int32
     lib.pkv_lse_combine.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int32, c_void_p, c_int64, c_void_p]
     lib.pkv_polar_scores.restype = c_int32

@@ -141,6 +141,20 @@ class DeviceCodec:
         a.partial_out = partial_out.data_ptr() if partial_out is not None else None
         return a
 
+    def describe(self, q: torch.Tensor, k_codes: torch.Tensor, v_codes: torch.Tensor,
+                 num_splits: int = 0) -> dict:
+        """The kernel and split plan ``attention`` would use for these tensors (launches nothing)."""
+        if q.dim() == 4:
+            q = q[:, :, 0, :]
+        a = self._attn_args(q, k_codes, v_codes, self.dim ** -0.5, None, None, num_splits, None)
+        plan = _lib.PkvAttnPlan()
+        with torch.cuda.device(self.device):
+            rc = _lib.load().pkv_attn_describe(ctypes.byref(self.struct), ctypes.byref(a), ctypes.byref(plan))
+        _lib.check(rc, "pkv_attn_describe")
+        d = {f: int(getattr(plan, f)) for f, _ in plan._fields_}
+        d["kernel"] = _lib.KERNEL_NAMES[d["kernel"]]
+        return d
+
     def workspace(self, nbytes: int) -> torch.Tensor:
         """Per-stream workspace, zeroed once when (re)allocated; calls leave it zeroed."""
         key = self._stream()

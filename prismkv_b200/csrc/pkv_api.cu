@@ -14,6 +14,7 @@ int launch_encode(const pkv_codec* c, const void* x, int xdt, int64_t n, int64_t
 int launch_decode(const pkv_codec* c, const void* codes, int cb, int64_t n, int64_t cs, void* out, int odt,
                   int64_t os, cudaStream_t st);
 size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a);
+void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out);
 int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_lse_combine(const pkv_codec* c, const float* parts, int n_parts, int64_t part_stride, int rows,
                        float* out, int64_t out_rs, cudaStream_t st);
@@ -108,7 +109,7 @@ int pkv_decode(const pkv_codec* c, const void* codes, int32_t code_bytes, int64_
                               static_cast<cudaStream_t>(stream));
 }
 
-static int check_attn(const pkv_codec* c, const pkv_attn_args* a) {
+static int check_attn(const pkv_codec* c, const pkv_attn_args* a, bool need_out = true) {
     int rc = check_codec(c, false, true);
     if (rc) return rc;
     if (!a) return PKV_ERR_INVALID;
@@ -123,7 +124,7 @@ static int check_attn(const pkv_codec* c, const pkv_attn_args* a) {
     if (a->num_splits < 0) return PKV_ERR_INVALID;
     if (a->batch == 0) return PKV_OK;
     if (!a->q || (a->seq_len > 0 && (!a->k_codes || !a->v_codes))) return PKV_ERR_INVALID;
-    if (a->partial_only ? !a->partial_out : !a->out) return PKV_ERR_INVALID;
+    if (need_out && (a->partial_only ? !a->partial_out : !a->out)) return PKV_ERR_INVALID;
     const int64_t m = c->dim / 3;
     if (a->kv_head_stride < (int64_t)a->seq_len * m || a->kv_batch_stride < 0) return PKV_ERR_INVALID;
     return PKV_OK;
@@ -132,6 +133,14 @@ static int check_attn(const pkv_codec* c, const pkv_attn_args* a) {
 size_t pkv_attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a) {
     if (check_attn(c, a) != PKV_OK || a->batch == 0) return 0;
     return pkv::attn_workspace_size(c, a);
+}
+
+int pkv_attn_describe(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out) {
+    if (!out) return PKV_ERR_INVALID;
+    const int rc = check_attn(c, a, false);     // output pointers are not needed to plan
+    if (rc) return rc;
+    pkv::describe_attn(c, a, out);
+    return PKV_OK;
 }
 
 int pkv_workspace_init(void* workspace, size_t bytes, void* stream) {

@@ -1266,6 +1266,16 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     return pl;
 }
 
+void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out) {
+    const AttnPlan pl = plan_attn(c, a);
+    out->kernel = pl.mha12 ? PKV_KERNEL_MHA12 : (pl.polar ? PKV_KERNEL_POLAR : PKV_KERNEL_LUT);
+    out->num_splits = pl.nsplit;
+    out->tokens_per_split = pl.chunk;
+    out->threads = pl.threads;
+    out->smem_bytes = pl.smem;
+    out->ctas_per_sm = pl.ctas_per_sm;
+}
+
 size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a) {
     AttnPlan pl = plan_attn(c, a);
     if (pl.nsplit <= 1) return 0;

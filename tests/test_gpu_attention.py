@@ -198,6 +198,21 @@ def test_attention_shapes_in_turn_share_workspace(cuda_ready):
         np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,S,variant,bits,kernel", [
+    (8, 32, 32, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),
+    (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_polar_kernel"),
+    (2, 8, 8, 4096, "v1", (3, 3, 2), "attn_polar_kernel"),
+    (2, 8, 8, 4096, "lloyd_bias", (4, 4, 4), "attn_polar_kernel"),
+    (2, 32, 8, 4096, "learned_bias", (4, 4, 4), "attn_lut_kernel"),
+])
+def test_attention_plan_picks_kernel(cuda_ready, B, Hq, Hkv, S, variant, bits, kernel):
+    q, _ = _setup(variant, bits)
+    kc = torch.zeros(B, Hkv, S, q.m, dtype=q.code_dtype, device=DEV)
+    plan = q.codec(torch.device(DEV)).describe(torch.zeros(B, Hq, 96, device=DEV), kc, kc)
+    assert plan["kernel"] == kernel
+    assert plan["num_splits"] >= 1 and plan["smem_bytes"] <= 227 * 1024
+
+
 def test_phi3_decode_full_size(cuda_ready):
     """The benchmark workload at full size (B=8, 32 heads, S=4096) against the oracle."""
     from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
