@@ -189,55 +189,94 @@ def cpu_reference_bandwidth(w, kc, vc, q, R, budget_s=12.0, tokens=None):
 # GPU decode benchmark
 # ---------------------------------------------------------------------------
 
+def _partition(w, ws, rank):
+    """How N ranks share the workload: replicas, batch shards or sequence shards."""
+    from prismkv_b200.dist import shard_range
+    if ws > 1 and w.name == "longctx-splitseq":
+        a, b = shard_range(w.seq_len, ws, rank)
+        return "sequence", w.scaled(seq_len=b - a), (a, b)
+    if ws > 1 and w.name == "aggressive-332":
+        a, b = shard_range(w.batch, ws, rank)
+        return "batch", w.scaled(batch=b - a), (a, b)
+    return "replicas", w, None
+
+
 def bench_decode(args, ws, rank, device):
     from prismkv_b200 import _lib, decode_attention
+    from prismkv_b200.dist import gather_partials, split_sequence_decode
     from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
 
     w = WORKLOADS[args.workload]
+    mode, lw, span = _partition(w, ws, rank)
     quant = make_quantizer(w)
     codec = quant.codec(device)
-    kc, vc = make_kv_codes(w, quant, device, seed=rank)
-    q = make_query(w, device, seed=100 + rank)
-    out = torch.empty(w.batch, w.q_heads, w.dim, dtype=torch.float32, device=device)
+    kc, vc = make_kv_codes(lw, quant, device, seed=rank)
+    if mode == "replicas":
+        q = make_query(w, device, seed=100 + rank)
+    elif mode == "batch":
+        q = make_query(w, device, seed=100)[span[0]:span[1]].contiguous()
+    else:
+        q = make_query(w, device, seed=100)
+    B, Hq, D = q.shape
+    out = torch.empty(B, Hq, D, dtype=torch.float32, device=device)
     scrub = L2Scrub(device)
     stream = torch.cuda.current_stream(device)
-
     plan = codec.describe(q, kc, vc)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
 
-    def step():
-        codec.attention(q, kc, vc, out=out)
+    def step(i=None):
+        if i is not None:
+            starts[i].record(stream)
+        if mode == "sequence":
+            # split_sequence_decode, spelled out to time the attention kernel on its own
+            part = codec.attention(q, kc, vc, partial=True)
+            if i is not None:
+                mids[i].record(stream)
+            codec.combine(gather_partials(part.view(B * Hq, D + 2)), out=out.view(B * Hq, D))
+        else:
+            codec.attention(q, kc, vc, out=out)
+        if i is not None:
+            ends[i].record(stream)
 
     for _ in range(args.warmup):
         scrub()
         step()
     torch.cuda.synchronize(device)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     _barrier(ws)
     torch.cuda.synchronize(device)
     with ClockSampler(device.index) as clk:
         wall0 = time.perf_counter()
         for i in range(args.steps):
             scrub()
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
+            step(i)
         torch.cuda.synchronize(device)
         wall = time.perf_counter() - wall0
     _barrier(ws)
-    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]          # ms, attention kernel only
-    local_ms = sum(times) / len(times)
+    step_ms = [s_.elapsed_time(e) for s_, e in zip(starts, ends)]
+    if mode == "sequence":                                                  # the attention kernel alone
+        kern_ms = [s_.elapsed_time(m) for s_, m in zip(starts, mids)]
+    else:
+        kern_ms = step_ms
+    local_ms = sum(step_ms) / len(step_ms)
+    local_kern_ms = sum(kern_ms) / len(kern_ms)
     ms = _max_over_ranks(local_ms, ws, device)
     if _lib.device_error() != 0:
         raise RuntimeError("device error flag set during the benchmark")
 
-    nbytes = w.decode_bytes()
-    total_bytes = nbytes * ws
+    local_bytes = lw.decode_bytes()
+    if mode == "replicas":
+        total_bytes = local_bytes * ws
+    elif mode == "batch":
+        total_bytes = w.decode_bytes()
+    else:                                  # every rank reads its codes and the query, writes the output
+        total_bytes = w.kv_code_bytes() + ws * (local_bytes - lw.kv_code_bytes())
     value = total_bytes / (ms * 1e-3) / 1e9
-    achieved = nbytes / (local_ms * 1e-3) / 1e9
+    achieved = local_bytes / (local_kern_ms * 1e-3) / 1e9
     peak, peak_kind = _peaks()
 
-    # end to end through the public API: pinned host inputs -> device -> kernel -> host output
+    # end to end through the public API: pinned host inputs -> device -> kernel(s) -> host output
     e2e_steps = max(3, min(args.steps, 20))
     h_kc = kc.cpu().pin_memory()
     h_vc = vc.cpu().pin_memory()
@@ -249,7 +288,10 @@ def bench_decode(args, ws, rank, device):
         d_kc.copy_(h_kc, non_blocking=True)
         d_vc.copy_(h_vc, non_blocking=True)
         d_q.copy_(h_q, non_blocking=True)
-        o = decode_attention(quant, d_q, d_kc, d_vc)
+        if mode == "sequence":
+            o = split_sequence_decode(quant, d_q, d_kc, d_vc)
+        else:
+            o = decode_attention(quant, d_q, d_kc, d_vc)
         h_out.copy_(o, non_blocking=True)
 
     for _ in range(2):
@@ -267,28 +309,34 @@ def bench_decode(args, ws, rank, device):
     h2d = h_kc.numel() * h_kc.element_size() + h_vc.numel() * h_vc.element_size() + h_q.numel() * h_q.element_size()
     d2h = h_out.numel() * h_out.element_size()
 
+    parallelism = {"replicas": f"replicas x{ws}", "batch": f"batch-sharded x{ws} (no collective)",
+                   "sequence": f"sequence-sharded x{ws} (NCCL all-gather of partials + LSE combine)"}[mode]
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak" if mode == "replicas" else "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": w.name, "batch": w.batch, "q_heads": w.q_heads, "kv_heads": w.kv_heads,
                    "seq_len": w.seq_len, "head_dim": w.dim, "bits": "+".join(map(str, w.bits)),
                    "codes": "uint8" if w.code_bytes == 1 else "uint16",
                    "codebook": "learned+bias" if w.learned else "uniform-polar",
                    "q_dtype": str(w.q_dtype).replace("torch.", ""),
-                   "bytes_per_step": nbytes, "l2": L2Scrub.DESCRIPTION,
-                   "parallelism": f"replicas x{ws}"},
+                   "bytes_per_step": total_bytes, "l2": L2Scrub.DESCRIPTION,
+                   "parallelism": parallelism},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": _committed_traffic(plan["kernel"], w.name),
-                     "kernel": plan["kernel"], "num_splits": plan["num_splits"]},
-        "e2e": {"value": round(nbytes * ws / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+                     "traffic": _committed_traffic(plan["kernel"], w.name) if mode == "replicas" else None,
+                     "kernel": plan["kernel"], "num_splits": plan["num_splits"],
+                     "balanced": bool(plan["balanced"])},
+        "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if mode == "sequence" else 1),
         "clocks": clk.summary(),
         "wall_s_timed": round(wall, 4),
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if mode == "sequence":
+        line["attn_ms_per_step"] = round(local_kern_ms, 5)
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         gbs, per, tokens, reps = cpu_reference_bandwidth(w, kc, vc, q, quant.R)
         line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
                                 "sample": f"one (batch, kv-head) slice of {tokens} tokens x {w.q_heads // w.kv_heads} "

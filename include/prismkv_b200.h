@@ -163,6 +163,9 @@ typedef struct pkv_attn_plan {
     int32_t threads;           /* per CTA                                       */
     int32_t smem_bytes;        /* dynamic shared memory per CTA                 */
     int32_t ctas_per_sm;       /* residency the schedule is planned for         */
+    int32_t balanced;          /* 1: every CTA streams an equal share of token
+                                  tiles (num_splits = partial slots per row);
+                                  0: round-robin over (batch, kv head, split)  */
 } pkv_attn_plan;
 PKV_API int pkv_attn_describe(const pkv_codec *c, const pkv_attn_args *a, pkv_attn_plan *out);
 

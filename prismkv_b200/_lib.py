@@ -47,7 +47,7 @@ class PkvAttnArgs(ctypes.Structure):
 
 class PkvAttnPlan(ctypes.Structure):
     _fields_ = [("kernel", c_int32), ("num_splits", c_int32), ("tokens_per_split", c_int32),
-                ("threads", c_int32), ("smem_bytes", c_int32), ("ctas_per_sm", c_int32)]
+                ("threads", c_int32), ("smem_bytes", c_int32), ("ctas_per_sm", c_int32), ("balanced", c_int32)]
 
 
 KERNEL_NAMES = {1: "attn_mha12_kernel", 2: "attn_polar_kernel", 3: "attn_lut_kernel"}

@@ -58,6 +58,11 @@ struct AttnParams {
     int bits_flat, code_mask, flat_mask, xy_per_z, n_xy, Cz;
     float r_max;
     int num_items, stages;
+    // balanced schedule (bal != 0): CTA c streams global tiles [c T / G, (c+1) T / G) of the
+    // unit-major tile sequence; segments are cut at unit ends, at every `seg_cap` tiles of a
+    // unit and at CTA boundaries.  slots: partial rows kept per (b, q head) in the workspace.
+    int bal, tt, tpu, seg_cap, slots;
+    int64_t tiles;
 };
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -68,10 +73,13 @@ __device__ __forceinline__ float q_load(const void* q, int qdt, int64_t idx) {
     return __half2float(__ldg(static_cast<const __half*>(q) + idx));
 }
 
-struct ItemRange { int b, hk, split, tok0, tok1; };
+// One segment of work: tokens [tok0, tok1) of (b, kv head hk).  The unit's
+// segments number nseg; this one writes partial slot `split` when nseg > 1.
+struct ItemRange { int b, hk, split, tok0, tok1, nseg; };
 
 __device__ __forceinline__ ItemRange item_range(const AttnParams& p, int item) {
     ItemRange r;
+    r.nseg = p.nsplit;
     r.split = item % p.nsplit;
     int bh = item / p.nsplit;
     r.hk = bh % p.Hkv;
@@ -81,6 +89,58 @@ __device__ __forceinline__ ItemRange item_range(const AttnParams& p, int item) {
     r.tok1 = min(L, r.tok0 + p.chunk);
     if (r.tok1 < r.tok0) r.tok1 = r.tok0;
     return r;
+}
+
+// Cut points strictly inside unit tiles [a, b): chunk cuts a + k seg_cap and the
+// CTA boundaries floor(c T / G).  slot = cuts in (a, t]; nseg = 1 + cuts in (a, b).
+__device__ inline void balanced_slot(const AttnParams& p, int64_t a, int64_t b, int64_t t, int G, int& slot,
+                                     int& nseg) {
+    const int64_t T = p.tiles, cap = p.seg_cap;
+    int in_unit = (int)((b - a - 1) / cap), upto_t = (int)((t - a) / cap);
+    for (int64_t c = ((a + 1) * G + T - 1) / T; c < G; ++c) {
+        const int64_t cut = c * T / G;
+        if (cut >= b) break;
+        if ((cut - a) % cap != 0) {
+            ++in_unit;
+            if (cut <= t) ++upto_t;
+        }
+    }
+    slot = upto_t;
+    nseg = 1 + in_unit;
+}
+
+// Work cursor shared by the producer and the consumers of a CTA: both walk the
+// same segment sequence.  Round-robin items (bal == 0) or the balanced tile range.
+struct WorkCursor { int64_t t, t_end; int item; };
+
+__device__ __forceinline__ WorkCursor work_begin(const AttnParams& p) {
+    WorkCursor c;
+    c.item = blockIdx.x;
+    c.t = (int64_t)blockIdx.x * p.tiles / gridDim.x;
+    c.t_end = (int64_t)(blockIdx.x + 1) * p.tiles / gridDim.x;
+    return c;
+}
+
+// BAL = false compiles the balanced branch out (kernels the planner never balances).
+template <bool BAL>
+__device__ inline bool work_next(const AttnParams& p, WorkCursor& c, ItemRange& r) {
+    if (!BAL || !p.bal) {
+        if (c.item >= p.num_items) return false;
+        r = item_range(p, c.item);
+        c.item += gridDim.x;
+        return true;
+    }
+    if (c.t >= c.t_end) return false;
+    const int64_t u = c.t / p.tpu, a = u * p.tpu, b = a + p.tpu;
+    const int64_t cb = a + ((c.t - a) / p.seg_cap + 1) * p.seg_cap;
+    const int64_t e = min(c.t_end, min(b, cb));
+    r.hk = (int)(u % p.Hkv);
+    r.b = (int)(u / p.Hkv);
+    r.tok0 = (int)(c.t - a) * p.tt;
+    r.tok1 = min(p.S, (int)(e - a) * p.tt);
+    balanced_slot(p, a, b, c.t, gridDim.x, r.split, r.nseg);
+    c.t = e;
+    return true;
 }
 
 // transpose-reduce: on entry each lane holds v[0..31]; on exit v[0] of lane l
@@ -156,10 +216,10 @@ __device__ __forceinline__ void rotate_query(const AttnParams& p, const ItemRang
 // rotated-space output).  Writes the partial row, or merges splits and writes
 // out = (o / l) @ R.  All `nthr` consumer threads call it; barrier id 1.
 __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float* sM, const float* sL,
-                            const float* sO, float* sFin, int* sflag, const float* Rp, int pitch, int tid,
-                            int nthr) {
+                            float* sO, float* sFin, int* sflag, const float* Rp, int pitch, int tid,
+                            int nthr, int max_parts) {
     const int dim = p.dim, greal = p.G;
-    const bool single = (p.nsplit == 1);
+    const bool single = (r.nseg == 1);
     bool finalize = single && !p.partial_only;
     for (int idx = tid; idx < greal * (dim + 2); idx += nthr) {
         const int g = idx / (dim + 2), k = idx % (dim + 2);
@@ -173,7 +233,7 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
                 float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
                 dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : val;
             } else {
-                float* dst = p.ws_part + (((int64_t)r.b * p.Hq + hq) * p.nsplit + r.split) * (dim + 2);
+                float* dst = p.ws_part + (((int64_t)r.b * p.Hq + hq) * p.slots + r.split) * (dim + 2);
                 dst[k] = val;
             }
         }
@@ -184,7 +244,7 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
         if (tid == 0) {
             int32_t* cnt = p.ws_count + (r.b * p.Hkv + r.hk);
             const int prev = atomicAdd(cnt, 1);
-            const int last = (prev == p.nsplit - 1);
+            const int last = (prev == r.nseg - 1);
             if (last) { __threadfence(); atomicExch(cnt, 0); }
             sflag[0] = last;
         }
@@ -193,11 +253,11 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
             for (int idx = tid; idx < greal * (dim + 2); idx += nthr) {
                 const int g = idx / (dim + 2), k = idx % (dim + 2);
                 const int hq = r.hk * greal + g;
-                const float* src = p.ws_part + ((int64_t)r.b * p.Hq + hq) * p.nsplit * (dim + 2);
+                const float* src = p.ws_part + ((int64_t)r.b * p.Hq + hq) * p.slots * (dim + 2);
                 float M = -INFINITY;
-                for (int sp = 0; sp < p.nsplit; ++sp) M = fmaxf(M, __ldcg(src + sp * (dim + 2)));
+                for (int sp = 0; sp < r.nseg; ++sp) M = fmaxf(M, __ldcg(src + sp * (dim + 2)));
                 float v = 0.f, lsw = 0.f;
-                for (int sp = 0; sp < p.nsplit; ++sp) {
+                for (int sp = 0; sp < r.nseg; ++sp) {
                     const float ms = __ldcg(src + sp * (dim + 2));
                     const float f = (ms == -INFINITY) ? 0.f : fast_exp2(ms - M);
                     lsw = fmaf(__ldcg(src + sp * (dim + 2) + 1), f, lsw);
@@ -213,26 +273,59 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
             // Clear the consumed partials: a workspace shared by calls of other shapes puts its
             // counters at other offsets, so every byte must be zero again after each call.
             named_bar_sync(1, nthr);
-            float* rows = p.ws_part + ((int64_t)r.b * p.Hq + (int64_t)r.hk * greal) * p.nsplit * (dim + 2);
-            for (int idx = tid; idx < greal * p.nsplit * (dim + 2); idx += nthr) rows[idx] = 0.f;
+            for (int g = 0; g < greal; ++g) {
+                float* rows = p.ws_part + ((int64_t)r.b * p.Hq + (int64_t)r.hk * greal + g) * p.slots * (dim + 2);
+                for (int k = tid; k < r.nseg * (dim + 2); k += nthr) rows[k] = 0.f;
+            }
             finalize = !p.partial_only;
         }
     }
     if (finalize) {
+        // out = fin @ R.  With parts > 1, up to max_parts threads share an output, each summing a
+        // slice of k with two chains; sO (at least max_parts * G * dim floats, dead by now) holds
+        // their partial sums.  With one part, each thread batches 16 loads of R ahead of its FMAs.
         named_bar_sync(1, nthr);
-        for (int idx = tid; idx < greal * dim; idx += nthr) {
-            const int g = idx / dim, i = idx % dim;
-            float v = 0.f;
-            for (int k0 = 0; k0 < dim; k0 += 16) {
-                float rv[16];
-                #pragma unroll
-                for (int u = 0; u < 16; ++u) rv[u] = (k0 + u < dim) ? Rp[(k0 + u) * pitch + i] : 0.f;
-                #pragma unroll
-                for (int u = 0; u < 16; ++u)
-                    if (k0 + u < dim) v = fmaf(sFin[g * dim + k0 + u], rv[u], v);
+        const int gd = greal * dim;
+        const int parts = max(1, min(max_parts, nthr / gd));
+        if (parts == 1) {
+            for (int idx = tid; idx < gd; idx += nthr) {
+                const int g = idx / dim, i = idx % dim;
+                float v = 0.f;
+                for (int k0 = 0; k0 < dim; k0 += 16) {
+                    float rv[16];
+                    #pragma unroll
+                    for (int u = 0; u < 16; ++u) rv[u] = (k0 + u < dim) ? Rp[(k0 + u) * pitch + i] : 0.f;
+                    #pragma unroll
+                    for (int u = 0; u < 16; ++u)
+                        if (k0 + u < dim) v = fmaf(sFin[g * dim + k0 + u], rv[u], v);
+                }
+                const int hq = r.hk * greal + g;
+                p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
             }
-            const int hq = r.hk * greal + g;
-            p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
+        }
+        const int klen = (dim + parts - 1) / parts;
+        for (int idx = tid; parts > 1 && idx < gd * parts; idx += nthr) {
+            const int part = idx / gd, gi = idx % gd, g = gi / dim, i = gi % dim;
+            const int k1 = min(dim, (part + 1) * klen);
+            const float* f = sFin + g * dim;
+            float v0 = 0.f, v1 = 0.f;
+            int k = part * klen;
+            #pragma unroll 8
+            for (; k + 1 < k1; k += 2) {
+                v0 = fmaf(f[k], Rp[k * pitch + i], v0);
+                v1 = fmaf(f[k + 1], Rp[(k + 1) * pitch + i], v1);
+            }
+            if (k < k1) v0 = fmaf(f[k], Rp[k * pitch + i], v0);
+            sO[idx] = v0 + v1;
+        }
+        if (parts > 1) {
+            named_bar_sync(1, nthr);
+            for (int gi = tid; gi < gd; gi += nthr) {
+                float v = 0.f;
+                for (int part = 0; part < parts; ++part) v += sO[part * gd + gi];
+                const int g = gi / dim, i = gi % dim, hq = r.hk * greal + g;
+                p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
+            }
         }
     }
     named_bar_sync(1, nthr);     // shared scratch is reused by the next item
@@ -240,14 +333,15 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
 
 // Producer loop: for every item, `passes` sweeps over its token range (K then V
 // for the two-pass kernel; K+V tiles together for the one-pass kernel).
-template <int TT, bool KV_TOGETHER>
+template <int TT, bool KV_TOGETHER, bool BAL>
 __device__ void produce(const AttnParams& p, uint8_t* stage_base, int stage_bytes, uint64_t* full,
                         uint64_t* empty, int ncons_warps, int code_bytes) {
     const uint32_t row_bytes = (uint32_t)(p.m * code_bytes);
     int seq = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
-        const ItemRange r = item_range(p, item);
+    WorkCursor wc = work_begin(p);
+    ItemRange r;
+    while (ok && work_next<BAL>(p, wc, r)) {
         const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.hk * p.kv_hs) * code_bytes;
         for (int pass = 0; pass < (KV_TOGETHER ? 1 : 2) && ok; ++pass) {
             for (int t0 = r.tok0; t0 < r.tok1; t0 += TT, ++seq) {
@@ -367,7 +461,7 @@ __global__ void __launch_bounds__(kPW * 32 + 32, 2) attn_polar_kernel(AttnParams
     __syncthreads();
 
     if (warp == kPW) {
-        if (lane == 0) produce<kPTT, false>(p, smem + L.off_stage, L.stage_bytes, full, empty, kPW, CB);
+        if (lane == 0) produce<kPTT, false, false>(p, smem + L.off_stage, L.stage_bytes, full, empty, kPW, CB);
         return;
     }
 
@@ -375,8 +469,9 @@ __global__ void __launch_bounds__(kPW * 32 + 32, 2) attn_polar_kernel(AttnParams
     const int myh = lane / TB, myt = lane % TB;
     int seq = 0;
     bool alive = true;
-    for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
-        const ItemRange r = item_range(p, item);
+    WorkCursor wc = work_begin(p);
+    ItemRange r;
+    while (work_next<false>(p, wc, r)) {
         const int ntok = r.tok1 - r.tok0;
         const int ntiles = (ntok + kPTT - 1) / kPTT;
         rotate_query<G>(p, r, p.R, dim, sQ, sFin, tid, nthr);
@@ -535,7 +630,7 @@ __global__ void __launch_bounds__(kPW * 32 + 32, 2) attn_polar_kernel(AttnParams
             sAcc[idx] = v;                      // warp 0's slot now holds the sum
         }
         named_bar_sync(1, nthr);
-        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, dim, tid, nthr);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, dim, tid, nthr, 4);
     }
 }
 
@@ -668,13 +763,15 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
     }
     // the first item's query, ahead of the code stream too
     float qreg = 0.f;
-    if (blockIdx.x < p.num_items && tid < 96) {
-        const ItemRange r = item_range(p, blockIdx.x);
-        qreg = q_load(p.q, p.qdt, (int64_t)r.b * p.q_bs + (int64_t)r.hk * p.q_hs + tid);
+    {
+        WorkCursor pc = work_begin(p);
+        ItemRange r0;
+        if (tid < 96 && work_next<false>(p, pc, r0))
+            qreg = q_load(p.q, p.qdt, (int64_t)r0.b * p.q_bs + (int64_t)r0.hk * p.q_hs + tid);
     }
     __syncthreads();
     if (warp == W) {
-        if (lane == 0) produce<TT, false>(p, smem, TILE, full, empty, W, 2);
+        if (lane == 0) produce<TT, false, false>(p, smem, TILE, full, empty, W, 2);
         return;
     }
 
@@ -684,8 +781,9 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
     const int tg = lane >> 2, q4 = lane & 3;             // V: token-in-8, 8-triplet chunk
     int seq = 0, ruse = 0;
     bool alive = true;
-    for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
-        const ItemRange r = item_range(p, item);
+    WorkCursor wc = work_begin(p);
+    ItemRange r;
+    while (work_next<false>(p, wc, r)) {
         const int ntok = r.tok1 - r.tok0;
         const int ntiles = (ntok + TT - 1) / TT;
         if (tid < 96) sQraw[tid] = qreg;
@@ -782,11 +880,10 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
         ++ruse;
         // prefetch the next item's query
         {
-            const int nitem = item + gridDim.x;
-            if (nitem < p.num_items && tid < 96) {
-                const ItemRange rn = item_range(p, nitem);
+            WorkCursor pc = wc;
+            ItemRange rn;
+            if (tid < 96 && work_next<false>(p, pc, rn))
                 qreg = q_load(p.q, p.qdt, (int64_t)rn.b * p.q_bs + (int64_t)rn.hk * p.q_hs + tid);
-            }
         }
         float M = -INFINITY;
         #pragma unroll
@@ -883,7 +980,7 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
         }
         if (alive && !mbar_wait(rbar, ruse & 1, kErrWaitFull)) alive = false;   // R back in place
         named_bar_sync(1, nthr);
-        finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 1);
     }
     // the last R copy must land before the CTA exits
     if (tid == 0 && alive) mbar_wait(rbar, ruse & 1, kErrWaitDrain);
@@ -967,7 +1064,7 @@ __global__ void __launch_bounds__(TMA ? kLW * 32 + 32 : kLW * 32) attn_lut_kerne
     __syncthreads();
 
     if (TMA && warp == kLW) {
-        if (lane == 0) produce<kLTT, true>(p, smem + L.off_stage, L.stage_bytes, full, empty, kLW, CB);
+        if (lane == 0) produce<kLTT, true, true>(p, smem + L.off_stage, L.stage_bytes, full, empty, kLW, CB);
         return;
     }
 
@@ -975,8 +1072,9 @@ __global__ void __launch_bounds__(TMA ? kLW * 32 + 32 : kLW * 32) attn_lut_kerne
     const int myh = lane / TB, myt = lane % TB;
     int seq = 0;
     bool alive = true;
-    for (int item = blockIdx.x; item < p.num_items; item += gridDim.x) {
-        const ItemRange r = item_range(p, item);
+    WorkCursor wc = work_begin(p);
+    ItemRange r;
+    while (work_next<true>(p, wc, r)) {
         const int greal = p.G;
         rotate_query<G>(p, r, sR, pitch, sQ, sFin, tid, nthr);
         named_bar_sync(1, nthr);
@@ -1134,7 +1232,7 @@ __global__ void __launch_bounds__(TMA ? kLW * 32 + 32 : kLW * 32) attn_lut_kerne
             if (k == dim) { sL[g] = v; sM[g] = M; } else { sO[g * dim + k] = v; }
         }
         named_bar_sync(1, nthr);
-        finish_item(p, r, sM, sL, sO, sFin, sflag, sR, pitch, tid, nthr);
+        finish_item(p, r, sM, sL, sO, sFin, sflag, sR, pitch, tid, nthr, 1);
     }
 }
 
@@ -1191,6 +1289,9 @@ struct AttnPlan {
     bool polar;                        // attn_polar_kernel, else attn_lut_kernel
     int G, TPL, stages, nsplit, chunk, tt, threads, smem, ctas_per_sm;
     bool tma;
+    bool bal;                          // balanced tile ranges instead of round-robin items
+    int tpu, seg_cap, slots;           // tiles per unit, tiles per segment at most, partial slots
+    int64_t tiles, grid;               // balanced: total tiles, CTAs
 };
 
 static bool tma_ok(const pkv_codec* c, const pkv_attn_args* a) {
@@ -1263,6 +1364,31 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     if (best == 0) best = (tiles_total + max_tiles_item - 1) / max_tiles_item;
     pl.chunk = ((tiles_total + best - 1) / best) * pl.tt;
     pl.nsplit = std::max(1, (a->seq_len + pl.chunk - 1) / pl.chunk);
+    pl.slots = pl.nsplit;
+    pl.bal = false;
+    // balanced schedule: every CTA streams the same number of tiles (uniform lengths only); a
+    // CTA's range spans at most ceil(per / cap) + 1 segments, each paying the item overhead
+    // Measured on B200: it pays for the one-pass LUT kernel, whose items carry no per-item
+    // score pass; the two-pass kernels' per-item fixed cost (~6 us) outweighs the balance.
+    if (!pl.polar && a->seq_lens == nullptr && a->num_splits == 0 && a->seq_len > 0) {
+        const int64_t T = units * tiles_total;
+        const int64_t G = std::min<int64_t>(grid, T);
+        const int64_t per = (T + G - 1) / G;
+        const int cap = std::min(max_tiles_item, tiles_total);
+        const double cost = (double)per + (double)((per + cap - 1) / cap + 1) + 0.25;
+        if (cost < best_cost - 1e-9) {
+            pl.bal = true;
+            pl.tpu = tiles_total;
+            pl.seg_cap = max_tiles_item;
+            pl.tiles = T;
+            pl.grid = G;
+            // cuts inside one unit: chunk ends plus CTA boundaries (at least T / G tiles apart)
+            const int64_t spacing = std::max<int64_t>(1, T / G);
+            pl.slots = (int)((tiles_total - 1) / max_tiles_item + 1 + (tiles_total - 1) / spacing + 1);
+            pl.nsplit = pl.slots;
+            pl.chunk = std::min(max_tiles_item, tiles_total) * pl.tt;
+        }
+    }
     return pl;
 }
 
@@ -1271,6 +1397,7 @@ void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* ou
     out->kernel = pl.mha12 ? PKV_KERNEL_MHA12 : (pl.polar ? PKV_KERNEL_POLAR : PKV_KERNEL_LUT);
     out->num_splits = pl.nsplit;
     out->tokens_per_split = pl.chunk;
+    out->balanced = pl.bal ? 1 : 0;
     out->threads = pl.threads;
     out->smem_bytes = pl.smem;
     out->ctas_per_sm = pl.ctas_per_sm;
@@ -1278,8 +1405,8 @@ void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* ou
 
 size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a) {
     AttnPlan pl = plan_attn(c, a);
-    if (pl.nsplit <= 1) return 0;
-    size_t part = (size_t)a->batch * a->q_heads * pl.nsplit * (c->dim + 2) * sizeof(float);
+    if (!pl.bal && pl.nsplit <= 1) return 0;
+    size_t part = (size_t)a->batch * a->q_heads * pl.slots * (c->dim + 2) * sizeof(float);
     part = (part + 255) / 256 * 256;
     return part + (size_t)a->batch * a->kv_heads * sizeof(int32_t);
 }
@@ -1292,8 +1419,9 @@ static int launch_kernel(K kern, const AttnParams& p, const AttnPlan& pl, cudaSt
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, pl.threads, pl.smem) != cudaSuccess ||
         per_sm <= 0)
         return PKV_ERR_CUDA;
-    const int grid = (int)std::min<int64_t>(p.num_items, (int64_t)per_sm * num_sms());
-    kern<<<grid, pl.threads, pl.smem, st>>>(p);
+    int64_t grid = std::min<int64_t>(p.num_items, (int64_t)per_sm * num_sms());
+    if (pl.bal) grid = std::min<int64_t>(grid, pl.grid);     // the partition the slots were sized for
+    kern<<<(unsigned)grid, pl.threads, pl.smem, st>>>(p);
     return cudaGetLastError() == cudaSuccess ? PKV_OK : PKV_ERR_CUDA;
 }
 
@@ -1350,10 +1478,13 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
     p.out = a->out; p.out_bs = a->out_batch_stride; p.out_hs = a->out_head_stride;
     p.nsplit = pl.nsplit; p.chunk = pl.chunk;
     p.partial_only = a->partial_only; p.partial_out = a->partial_out;
-    if (pl.nsplit > 1) {
+    p.bal = pl.bal ? 1 : 0;
+    p.slots = pl.slots;
+    p.tt = pl.tt; p.tpu = pl.tpu; p.seg_cap = pl.seg_cap; p.tiles = pl.bal ? pl.tiles : 0;
+    if (pl.bal || pl.nsplit > 1) {
         size_t need = attn_workspace_size(c, a);
         if (!ws || ws_bytes < need) return PKV_ERR_WORKSPACE;
-        size_t part = (size_t)a->batch * a->q_heads * pl.nsplit * (c->dim + 2) * sizeof(float);
+        size_t part = (size_t)a->batch * a->q_heads * pl.slots * (c->dim + 2) * sizeof(float);
         part = (part + 255) / 256 * 256;
         p.ws_part = static_cast<float*>(ws);
         p.ws_count = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + part);
@@ -1367,7 +1498,7 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
     p.Cz = 1 << c->bits_z;
     p.n_xy = (c->xy_per_z ? p.Cz : 1) << p.bits_flat;
     p.r_max = c->r_max;
-    p.num_items = a->batch * a->kv_heads * pl.nsplit;
+    p.num_items = pl.bal ? (int)std::min<int64_t>(pl.tiles, INT32_MAX) : a->batch * a->kv_heads * pl.nsplit;
     p.stages = pl.stages;
     if (p.num_items == 0) return PKV_OK;
     if (pl.mha12) return launch_kernel(attn_mha12_kernel, p, pl, st);

@@ -105,10 +105,15 @@ def _kv_rows(w: Workload, g: torch.Generator, device, rows: int, head_of_row: to
 
 def make_kv_codes(w: Workload, quantizer: StackedPlaneQuantizer, device, seed: int = 0,
                   chunk_rows: int = 1 << 21) -> Tuple[torch.Tensor, torch.Tensor]:
-    """(B, Hkv, S, m) packed K and V codes: Gaussian vectors encoded on the GPU in chunks."""
+    """(B, Hkv, S, m) packed K and V codes: Gaussian vectors encoded on the GPU in chunks.
+
+    ``seed`` draws the vectors.  The per-head scales and the outlier channels are a
+    property of the workload, fixed across seeds, so that shards drawn with different
+    seeds on different ranks belong to one cache.
+    """
     device = torch.device(device)
     g = torch.Generator(device=device).manual_seed(seed)
-    gh = torch.Generator().manual_seed(seed + 1)
+    gh = torch.Generator().manual_seed(1)
     scales = (0.5 + 1.5 * torch.rand(w.kv_heads, generator=gh)).to(device) if w.head_scale else None
     outlier = None
     if w.outliers:

@@ -213,6 +213,26 @@ def test_attention_plan_picks_kernel(cuda_ready, B, Hq, Hkv, S, variant, bits, k
     assert plan["num_splits"] >= 1 and plan["smem_bytes"] <= 227 * 1024
 
 
+def test_attention_balanced_schedule(cuda_ready):
+    """Learned codebooks (one-pass kernel) over 128 KV heads x 4096 tokens: the planner gives
+    every CTA an equal share of token tiles, cutting segments across (batch, kv head) ends;
+    the segments merge through the workspace counters."""
+    q, p = _setup("learned_bias", (4, 4, 4))
+    B, Hq, Hkv, S = 16, 32, 8, 4096
+    kc, vc = _codes(q, B, Hkv, S, seed=31)
+    qv = torch.randn(B, Hq, 96, generator=torch.Generator(device=DEV).manual_seed(31), device=DEV)
+    codec = q.codec(torch.device(DEV))
+    plan = codec.describe(qv, kc, vc)
+    assert plan["kernel"] == "attn_lut_kernel" and plan["balanced"] == 1
+    ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64), vc.cpu().numpy().astype(np.int64),
+                           q.R.numpy(), p)
+    for _ in range(2):
+        out = decode_attention(q, qv, kc, vc)
+        np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+    from prismkv_b200 import _lib
+    assert _lib.device_error() == 0
+
+
 def test_phi3_decode_full_size(cuda_ready):
     """The benchmark workload at full size (B=8, 32 heads, S=4096) against the oracle."""
     from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
