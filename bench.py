@@ -346,11 +346,12 @@ def bench_decode(args, ws, rank, device):
 
 
 def bench_encode(args, ws, rank, device):
-    """learned-gqa encode: 32768 new tokens x 8 KV heads, K and V, bf16 in -> uint16 codes."""
+    """Encode of one layer's new tokens: 32768 tokens x kv heads, K and V, bf16 in -> packed codes
+    (learned-gqa: learned codebooks + BiasTable, 8 KV heads; phi3-decode: uniform polar, 32 heads)."""
     from prismkv_b200 import _lib
     from prismkv_b200.synthetic import WORKLOADS, make_encode_input, make_quantizer
 
-    w = WORKLOADS["learned-gqa"]
+    w = WORKLOADS[args.encode_workload]
     quant = make_quantizer(w)
     codec = quant.codec(device)
     tokens = 32768
@@ -381,11 +382,11 @@ def bench_encode(args, ws, rank, device):
         "metric": METRIC, "value": round(tokens * ws / (ms * 1e-3) / 1e6, 3), "unit": "Mtok/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "learned-gqa-encode", "tokens": tokens, "kv_heads": w.kv_heads, "head_dim": w.dim,
+        "config": {"workload": f"{w.name}-encode", "tokens": tokens, "kv_heads": w.kv_heads, "head_dim": w.dim,
                    "input": "bf16", "codes": "uint16", "bytes_per_step": nbytes},
         "roofline": {"bound": "hbm", "achieved": round(nbytes / (local_ms * 1e-3) / 1e9, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(nbytes / (local_ms * 1e-3) / 1e9 / peak, 4), "peak_kind": peak_kind,
-                     "traffic": _committed_traffic("encode_kernel", "learned-gqa"), "kernel": "pkv::encode_kernel"},
+                     "traffic": _committed_traffic("encode_kernel", w.name), "kernel": "pkv::encode_kernel"},
         "gpu_launches": args.steps, "clocks": clk.summary(),
     }
 
@@ -446,6 +447,7 @@ def main(argv=None):
     ap.add_argument("--impl", default="prismkv", choices=["prismkv", "reference"])
     ap.add_argument("--workload", default="phi3-decode")
     ap.add_argument("--mode", default="decode", choices=["decode", "encode"])
+    ap.add_argument("--encode-workload", default="learned-gqa", choices=["learned-gqa", "phi3-decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     if args.warmup < 3:

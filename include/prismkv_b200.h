@@ -94,6 +94,18 @@ typedef struct pkv_codec {
     const float *dec_z;
     const float *dec_xy;
     const float *bias_xy;                 /* (2^bits_z, 2) clamped BiasTable (x, y), or NULL */
+    /* Learned codebooks, optional: candidate centroids per cell of a
+     * cell_grid x cell_grid grid over [-cell_half_width, cell_half_width]^2
+     * per z-bin (cell_idx [2^bits_z][grid][grid][16] ascending indices,
+     * cell_cnt [2^bits_z][grid][grid], 255 = scan all).  NULL: full scan.  */
+    const uint8_t *cell_idx;
+    const uint8_t *cell_cnt;
+    int32_t cell_grid;
+    float cell_half_width;
+    /* Optional: R as three bf16 parts (3, dim, dim), R ~= R1 + R2 + R3 with
+     * R1 = bf16(R), R2 = bf16(R - R1), R3 = bf16(R - R1 - R2).  When set, bf16
+     * inputs of head_dim 96 are rotated on the tensor cores.                */
+    const void *R_bf16x3;
 } pkv_codec;
 
 /* ---- decode attention -------------------------------------------------- *
@@ -143,6 +155,22 @@ PKV_API int pkv_encode(const pkv_codec *c, const void *x, int32_t x_dtype, int64
 PKV_API int pkv_decode(const pkv_codec *c, const void *codes, int32_t code_bytes,
                int64_t n, int64_t code_stride, void *out, int32_t out_dtype,
                int64_t out_stride, void *stream);
+
+/* KV-cache forms of encode / decode.  The cache holds n_groups (batch x kv
+ * head) rows of token slots: slot t of group g at
+ * codes + (g * group_stride + t * code_stride) codes.
+ * pkv_encode_append encodes x rows (g, i) = x + (g * n_rows + i) * x_stride
+ * into slots pos + i of every group -- the device-side append that replaces
+ * the torch.cat of RawKVCache.update (cache/raw_cache.py:137-147) and
+ * PrismKVCache.update (cache/kv_cache.py:121-131).  pkv_decode_cache decodes
+ * slots [pos, pos + n_rows) of every group to out rows g * n_rows + i
+ * (RawKVCache.update's backend.decompress, raw_cache.py:150-159).        */
+PKV_API int pkv_encode_append(const pkv_codec *c, const void *x, int32_t x_dtype, int64_t n_groups,
+                      int64_t n_rows, int64_t x_stride, void *codes, int32_t code_bytes,
+                      int64_t group_stride, int64_t code_stride, int64_t pos, void *stream);
+PKV_API int pkv_decode_cache(const pkv_codec *c, const void *codes, int32_t code_bytes, int64_t n_groups,
+                     int64_t n_rows, int64_t group_stride, int64_t code_stride, int64_t pos,
+                     void *out, int32_t out_dtype, int64_t out_stride, void *stream);
 
 /* Bytes of workspace pkv_attn_decode needs for these arguments (0 when one
  * split per KV head suffices).  The workspace must be zeroed once

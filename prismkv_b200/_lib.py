@@ -23,7 +23,8 @@ DTYPE_CODES = {torch.float32: PKV_F32, torch.bfloat16: PKV_BF16, torch.float16: 
 
 EXPORTED = ("pkv_abi_version", "pkv_strerror", "pkv_device_error", "pkv_encode", "pkv_decode",
             "pkv_attn_workspace_size", "pkv_workspace_init", "pkv_attn_decode", "pkv_lse_combine",
-            "pkv_polar_scores", "pkv_attn_decode_noalloc", "pkv_attn_describe")
+            "pkv_polar_scores", "pkv_attn_decode_noalloc", "pkv_attn_describe", "pkv_encode_append",
+            "pkv_decode_cache")
 
 
 class PkvCodec(ctypes.Structure):
@@ -31,7 +32,9 @@ class PkvCodec(ctypes.Structure):
                 ("xy_mode", c_int32), ("xy_per_z", c_int32), ("z_nan_bin", c_int32), ("z_hi", c_float),
                 ("r_max", c_float), ("flags", c_int32),
                 ("R", c_void_p), ("z_thr", c_void_p), ("r2_thr", c_void_p), ("th_thr", c_void_p),
-                ("codebook", c_void_p), ("dec_z", c_void_p), ("dec_xy", c_void_p), ("bias_xy", c_void_p)]
+                ("codebook", c_void_p), ("dec_z", c_void_p), ("dec_xy", c_void_p), ("bias_xy", c_void_p),
+                ("cell_idx", c_void_p), ("cell_cnt", c_void_p), ("cell_grid", c_int32), ("cell_half_width", c_float),
+                ("R_bf16x3", c_void_p)]
 
 
 class PkvAttnArgs(ctypes.Structure):
@@ -68,6 +71,12 @@ def _declare(lib):
     lib.pkv_encode.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int64, c_void_p, c_int32, c_int64, c_void_p]
     lib.pkv_decode.restype = c_int32
     lib.pkv_decode.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int64, c_void_p, c_int32, c_int64, c_void_p]
+    lib.pkv_encode_append.restype = c_int32
+    lib.pkv_encode_append.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int64, c_int64, c_void_p, c_int32,
+                                      c_int64, c_int64, c_int64, c_void_p]
+    lib.pkv_decode_cache.restype = c_int32
+    lib.pkv_decode_cache.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int64, c_int64, c_int64, c_int64,
+                                     c_void_p, c_int32, c_int64, c_void_p]
     lib.pkv_attn_workspace_size.restype = c_size_t
     lib.pkv_attn_workspace_size.argtypes = [P(PkvCodec), P(PkvAttnArgs)]
     lib.pkv_workspace_init.restype = c_int32

@@ -43,6 +43,12 @@ class DeviceCodec:
             return torch.from_numpy(a).to(self.device)
 
         self._R = up(host.R)
+        # R as three bf16 parts for the tensor-core rotation (exact products, fp32 accumulation)
+        r = torch.from_numpy(np.ascontiguousarray(host.R, dtype=np.float32))
+        r1 = r.to(torch.bfloat16)
+        r2 = (r - r1.float()).to(torch.bfloat16)
+        r3 = (r - r1.float() - r2.float()).to(torch.bfloat16)
+        self._R_bf16x3 = torch.stack([r1, r2, r3]).contiguous().to(self.device)
         self._z_thr = up(host.z_thr)
         self._r2 = up(host.r2_thr)
         self._th = up(host.th_thr)
@@ -50,6 +56,10 @@ class DeviceCodec:
         self._dz = up(host.dec_z)
         self._dxy = up(host.dec_xy)
         self._bxy = up(host.bias_xy) if host.bias_xy is not None else None
+        self._cell_idx = self._cell_cnt = None
+        if host.cell_idx is not None:
+            self._cell_idx = torch.from_numpy(np.ascontiguousarray(host.cell_idx).reshape(-1)).to(self.device)
+            self._cell_cnt = torch.from_numpy(np.ascontiguousarray(host.cell_cnt).reshape(-1)).to(self.device)
         s = _lib.PkvCodec()
         s.dim = host.dim
         s.bits_z, s.bits_r, s.bits_theta = host.bits
@@ -67,6 +77,12 @@ class DeviceCodec:
         s.dec_z = self._dz.data_ptr()
         s.dec_xy = self._dxy.data_ptr()
         s.bias_xy = self._bxy.data_ptr() if self._bxy is not None else None
+        s.R_bf16x3 = self._R_bf16x3.data_ptr()
+        if self._cell_idx is not None:
+            s.cell_idx = self._cell_idx.data_ptr()
+            s.cell_cnt = self._cell_cnt.data_ptr()
+            s.cell_grid = host.cell_idx.shape[1]
+            s.cell_half_width = host.cell_half_width
         self.struct = s
         self._ws: Dict[int, torch.Tensor] = {}
         self.R = self._R.view(host.dim, host.dim)
@@ -96,6 +112,45 @@ class DeviceCodec:
                                 x.stride(0), out.data_ptr(), CODE_DTYPES[out.dtype], out.stride(0),
                                 self._stream())
         _lib.check(rc, "pkv_encode")
+        return out
+
+    def encode_append(self, x: torch.Tensor, cache: torch.Tensor, pos: int) -> None:
+        """Encode x (G, n, dim) into slots [pos, pos + n) of a (G, capacity, m) code cache."""
+        _lib.require_cuda(x, "vectors")
+        _lib.require_cuda(cache, "cache")
+        if x.dim() != 3 or x.shape[2] != self.dim or cache.dim() != 3 or cache.shape[0] != x.shape[0]:
+            raise ValueError("expected x (G, n, dim) and cache (G, capacity, m)")
+        if cache.shape[2] != self.m or cache.stride(2) != 1 or cache.stride(1) != self.m:
+            raise ValueError("cache rows must be compact (m codes per slot)")
+        G, n, _ = x.shape
+        if pos < 0 or pos + n > cache.shape[1]:
+            raise ValueError(f"slots [{pos}, {pos + n}) outside capacity {cache.shape[1]}")
+        if x.dtype not in _lib.DTYPE_CODES:
+            x = x.float()
+        x = x.contiguous()
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            rc = lib.pkv_encode_append(ctypes.byref(self.struct), x.data_ptr(), _lib.DTYPE_CODES[x.dtype], G, n,
+                                       self.dim, cache.data_ptr(), CODE_DTYPES[cache.dtype], cache.stride(0),
+                                       cache.stride(1), pos, self._stream())
+        _lib.check(rc, "pkv_encode_append")
+
+    def decode_cache(self, cache: torch.Tensor, pos: int, n: int,
+                     out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """Slots [pos, pos + n) of a (G, capacity, m) code cache -> (G, n, dim) vectors."""
+        _lib.require_cuda(cache, "cache")
+        if cache.dim() != 3 or cache.shape[2] != self.m or cache.stride(2) != 1:
+            raise ValueError("expected a (G, capacity, m) cache with unit code stride")
+        if pos < 0 or n < 0 or pos + n > cache.shape[1]:
+            raise ValueError(f"slots [{pos}, {pos + n}) outside capacity {cache.shape[1]}")
+        G = cache.shape[0]
+        out = torch.empty((G, n, self.dim), dtype=out_dtype, device=self.device)
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            rc = lib.pkv_decode_cache(ctypes.byref(self.struct), cache.data_ptr(), CODE_DTYPES[cache.dtype], G, n,
+                                      cache.stride(0), cache.stride(1), pos, out.data_ptr(),
+                                      _lib.DTYPE_CODES[out_dtype], self.dim, self._stream())
+        _lib.check(rc, "pkv_decode_cache")
         return out
 
     def decode(self, codes: torch.Tensor, out: Optional[torch.Tensor] = None,

@@ -10,9 +10,9 @@
 
 namespace pkv {
 int launch_encode(const pkv_codec* c, const void* x, int xdt, int64_t n, int64_t xs, void* codes, int cb,
-                  int64_t cs, cudaStream_t st);
+                  int64_t cs, int64_t group_rows, int64_t group_stride, cudaStream_t st);
 int launch_decode(const pkv_codec* c, const void* codes, int cb, int64_t n, int64_t cs, void* out, int odt,
-                  int64_t os, cudaStream_t st);
+                  int64_t os, int64_t group_rows, int64_t group_stride, cudaStream_t st);
 size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a);
 void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out);
 int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
@@ -93,7 +93,7 @@ int pkv_encode(const pkv_codec* c, const void* x, int32_t x_dtype, int64_t n, in
     if (!code_bits_fit(c, code_bytes)) return PKV_ERR_INVALID;
     if (n == 0) return PKV_OK;
     if (!x || !codes || x_stride < c->dim || code_stride < c->dim / 3) return PKV_ERR_INVALID;
-    return pkv::launch_encode(c, x, x_dtype, n, x_stride, codes, code_bytes, code_stride,
+    return pkv::launch_encode(c, x, x_dtype, n, x_stride, codes, code_bytes, code_stride, 0, 0,
                               static_cast<cudaStream_t>(stream));
 }
 
@@ -105,8 +105,48 @@ int pkv_decode(const pkv_codec* c, const void* codes, int32_t code_bytes, int64_
     if (!code_bits_fit(c, code_bytes)) return PKV_ERR_INVALID;
     if (n == 0) return PKV_OK;
     if (!codes || !out || out_stride < c->dim || code_stride < c->dim / 3) return PKV_ERR_INVALID;
-    return pkv::launch_decode(c, codes, code_bytes, n, code_stride, out, out_dtype, out_stride,
+    return pkv::launch_decode(c, codes, code_bytes, n, code_stride, out, out_dtype, out_stride, 0, 0,
                               static_cast<cudaStream_t>(stream));
+}
+
+// The code side of a KV cache: n_groups (batch x head) rows of `capacity`
+// token slots, group_stride codes apart.  Rows [pos, pos + n_rows) of each group.
+static int check_cache_rows(const pkv_codec* c, int64_t n_groups, int64_t n_rows, int64_t group_stride,
+                            int64_t code_stride, int64_t pos) {
+    if (n_groups < 0 || n_rows < 0 || pos < 0) return PKV_ERR_INVALID;
+    if (code_stride < c->dim / 3) return PKV_ERR_INVALID;
+    if (n_groups > 1 && group_stride < (pos + n_rows) * code_stride) return PKV_ERR_INVALID;
+    return PKV_OK;
+}
+
+int pkv_encode_append(const pkv_codec* c, const void* x, int32_t x_dtype, int64_t n_groups, int64_t n_rows,
+                      int64_t x_stride, void* codes, int32_t code_bytes, int64_t group_stride,
+                      int64_t code_stride, int64_t pos, void* stream) {
+    int rc = check_codec(c, true, false);
+    if (rc) return rc;
+    if (!valid_dtype(x_dtype) || !code_bits_fit(c, code_bytes)) return PKV_ERR_INVALID;
+    rc = check_cache_rows(c, n_groups, n_rows, group_stride, code_stride, pos);
+    if (rc) return rc;
+    if (n_groups * n_rows == 0) return PKV_OK;
+    if (!x || !codes || x_stride < c->dim) return PKV_ERR_INVALID;
+    uint8_t* first = static_cast<uint8_t*>(codes) + pos * code_stride * code_bytes;
+    return pkv::launch_encode(c, x, x_dtype, n_groups * n_rows, x_stride, first, code_bytes, code_stride, n_rows,
+                              group_stride, static_cast<cudaStream_t>(stream));
+}
+
+int pkv_decode_cache(const pkv_codec* c, const void* codes, int32_t code_bytes, int64_t n_groups, int64_t n_rows,
+                     int64_t group_stride, int64_t code_stride, int64_t pos, void* out, int32_t out_dtype,
+                     int64_t out_stride, void* stream) {
+    int rc = check_codec(c, false, true);
+    if (rc) return rc;
+    if (!valid_dtype(out_dtype) || !code_bits_fit(c, code_bytes)) return PKV_ERR_INVALID;
+    rc = check_cache_rows(c, n_groups, n_rows, group_stride, code_stride, pos);
+    if (rc) return rc;
+    if (n_groups * n_rows == 0) return PKV_OK;
+    if (!codes || !out || out_stride < c->dim) return PKV_ERR_INVALID;
+    const uint8_t* first = static_cast<const uint8_t*>(codes) + pos * code_stride * code_bytes;
+    return pkv::launch_decode(c, first, code_bytes, n_groups * n_rows, code_stride, out, out_dtype, out_stride,
+                              n_rows, group_stride, static_cast<cudaStream_t>(stream));
 }
 
 static int check_attn(const pkv_codec* c, const pkv_attn_args* a, bool need_out = true) {

@@ -39,7 +39,19 @@ struct CodecArgs {
     const void* in;            // x (encode) or codes (decode)
     void* out;                 // codes (encode) or vectors (decode)
     int64_t n, in_stride, out_stride;
+    // learned codebooks: candidate centroids per grid cell (cell_grid 0 = scan all K)
+    const uint8_t* cell_idx;
+    const uint8_t* cell_cnt;
+    int cell_grid;
+    float cell_lo, cell_scale;             // cell = floor((v - cell_lo) * cell_scale)
+    // code rows grouped as in a KV cache (0 = plain rows): code row n sits at
+    // (n / group_rows) * group_stride + (n % group_rows) * stride, in codes
+    int64_t group_rows, group_stride;
 };
+
+__device__ __forceinline__ int64_t code_row(const CodecArgs& a, int64_t n, int64_t stride) {
+    return a.group_rows > 0 ? (n / a.group_rows) * a.group_stride + (n % a.group_rows) * stride : n * stride;
+}
 
 // acc[rr][c] += sum_i A[row_rr][i] * B[i][col0 + c]    (A: [TR][lda], B: [K][kp])
 template <int MPT, int RPT>
@@ -99,6 +111,60 @@ __device__ __forceinline__ int nearest_centroid(const float2* __restrict__ cb, i
     return 0;
 }
 
+// The same argmin over the candidate list of the point's grid cell: candidates
+// are stored in ascending index order and include every centroid that can be
+// (or tie with) the nearest for any point of the cell, so the result equals the
+// full scan's.  Points outside the grid or in an overfull cell scan all K.
+constexpr int kCellMax = 16;
+
+__device__ __forceinline__ int nearest_centroid_cells(const CodecArgs& a, int iz, const float2* __restrict__ cb,
+                                                      float x, float y) {
+    if (a.cell_grid > 0 && isfinite(x) && isfinite(y)) {
+        const float fx = (x - a.cell_lo) * a.cell_scale, fy = (y - a.cell_lo) * a.cell_scale;
+        if (fx >= 0.f && fy >= 0.f && fx < (float)a.cell_grid && fy < (float)a.cell_grid) {
+            const int cell = (iz * a.cell_grid + (int)fy) * a.cell_grid + (int)fx;
+            const int n = __ldg(a.cell_cnt + cell);
+            if (n <= kCellMax) {
+                const uint8_t* cand = a.cell_idx + (size_t)cell * kCellMax;
+                float best = INFINITY;
+                int bi = 0;
+                for (int i = 0; i < n; ++i) {
+                    const int k = __ldg(cand + i);
+                    const float2 c = __ldg(cb + k);
+                    const float dx = x - c.x, dy = y - c.y;
+                    const float d2 = fmaf(dx, dx, dy * dy);
+                    if (d2 < best) { best = d2; bi = k; }
+                }
+                return bi;
+            }
+        }
+    }
+    return nearest_centroid(cb, a.K, x, y);
+}
+
+// Code of one rotated triplet (z, x, y): z bin by threshold count (NaN and
+// values >= z_hi as the reference's chain maps them), then the uniform polar
+// bins (r^2 and atan2 thresholds) or the nearest learned centroid of bin i_z.
+// thr: z | r^2 | theta thresholds, nz = 2^bits_z - 1, nr = 2^bits_r - 1.
+__device__ __forceinline__ uint32_t encode_triplet(const CodecArgs& a, const float* thr, int nz, int nr, float z,
+                                                   float xx, float yy) {
+    int iz;
+    if (isnan(z)) iz = a.z_nan_bin;
+    else if (z >= a.z_hi) iz = 0;
+    else iz = count_ge(thr, a.bits_z, z);
+    uint32_t flat;
+    if (a.xy_mode == 0) {
+        float s = __fadd_rn(__fmul_rn(xx, xx), __fmul_rn(yy, yy));
+        int ir = count_ge(thr + nz, a.bits_r, s);
+        int it = count_ge(thr + nz + nr, a.bits_t, atan2f(yy, xx));
+        flat = ((uint32_t)ir << a.bits_t) | (uint32_t)it;
+    } else {
+        const float2* cb = reinterpret_cast<const float2*>(a.codebook) + (size_t)iz * a.K;
+        flat = (uint32_t)nearest_centroid_cells(a, iz, cb, xx, yy);
+    }
+    return ((uint32_t)iz << a.bits_flat) | flat;
+}
+
 template <int MPT, int RPT, int XDT, int CB>
 __global__ void __launch_bounds__(256) encode_kernel(CodecArgs a) {
     constexpr int TR = 64 * RPT;
@@ -145,26 +211,13 @@ __global__ void __launch_bounds__(256) encode_kernel(CodecArgs a) {
             for (int rr = 0; rr < RPT; ++rr) {
                 int64_t n = n0 + row0 + 64 * rr;
                 if (n >= a.n) continue;
+                CT* crow = codes + code_row(a, n, a.out_stride);
                 #pragma unroll
                 for (int jj = 0; jj < MPT; ++jj) {
                     int j = j0 + jj;
                     if (j >= a.m) break;
-                    float z = acc[rr][3 * jj], xx = acc[rr][3 * jj + 1], yy = acc[rr][3 * jj + 2];
-                    int iz;
-                    if (isnan(z)) iz = a.z_nan_bin;
-                    else if (z >= a.z_hi) iz = 0;
-                    else iz = count_ge(thr, a.bits_z, z);
-                    uint32_t flat;
-                    if (a.xy_mode == 0) {
-                        float s = __fadd_rn(__fmul_rn(xx, xx), __fmul_rn(yy, yy));
-                        int ir = count_ge(thr + nz, a.bits_r, s);
-                        int it = count_ge(thr + nz + nr, a.bits_t, atan2f(yy, xx));
-                        flat = ((uint32_t)ir << a.bits_t) | (uint32_t)it;
-                    } else {
-                        const float2* cb = reinterpret_cast<const float2*>(a.codebook) + (size_t)iz * a.K;
-                        flat = (uint32_t)nearest_centroid(cb, a.K, xx, yy);
-                    }
-                    Code<CB>::store(codes + n * a.out_stride + j, ((uint32_t)iz << a.bits_flat) | flat);
+                    Code<CB>::store(crow + j, encode_triplet(a, thr, nz, nr, acc[rr][3 * jj], acc[rr][3 * jj + 1],
+                                                             acc[rr][3 * jj + 2]));
                 }
             }
         }
@@ -202,7 +255,7 @@ __global__ void __launch_bounds__(256) decode_kernel(CodecArgs a) {
             int64_t n = n0 + r;
             float z = 0.f, xx = 0.f, yy = 0.f;
             if (n < a.n) {
-                uint32_t c = Code<CB>::load(codes + n * a.in_stride + j) & mask;
+                uint32_t c = Code<CB>::load(codes + code_row(a, n, a.in_stride) + j) & mask;
                 z = __ldg(a.dec_z + (c >> a.bits_flat));
                 float2 xy = __ldg(dxy + (a.xy_per_z ? c : (c & fmask)));
                 xx = xy.x; yy = xy.y;
@@ -316,23 +369,38 @@ static void fill_args(CodecArgs& a, const pkv_codec* c) {
     a.z_hi = c->z_hi;
     a.R = c->R; a.z_thr = c->z_thr; a.r2_thr = c->r2_thr; a.th_thr = c->th_thr;
     a.codebook = c->codebook; a.dec_z = c->dec_z; a.dec_xy = c->dec_xy;
+    a.cell_grid = 0;
+    if (c->xy_mode == 1 && c->cell_idx && c->cell_cnt && c->cell_grid > 0 && c->cell_half_width > 0.f &&
+        (1 << (c->bits_r + c->bits_theta)) <= 256) {
+        a.cell_idx = c->cell_idx;
+        a.cell_cnt = c->cell_cnt;
+        a.cell_grid = c->cell_grid;
+        a.cell_lo = -c->cell_half_width;
+        a.cell_scale = (float)c->cell_grid / (2.f * c->cell_half_width);
+    }
 }
 
+int launch_encode_tc(const CodecArgs& a, int xdt, int cb, const void* r_bf16x3, cudaStream_t st);
+
 int launch_encode(const pkv_codec* c, const void* x, int xdt, int64_t n, int64_t xs,
-                  void* codes, int cb, int64_t cs, cudaStream_t st) {
+                  void* codes, int cb, int64_t cs, int64_t group_rows, int64_t group_stride, cudaStream_t st) {
     CodecArgs a{};
     fill_args(a, c);
     a.in = x; a.out = codes; a.n = n; a.in_stride = xs; a.out_stride = cs;
+    a.group_rows = group_rows; a.group_stride = group_stride;
+    const int rc = launch_encode_tc(a, xdt, cb, c->R_bf16x3, st);     // tensor cores where they apply
+    if (rc != PKV_ERR_UNSUPPORTED) return rc;
     if (a.m <= 32) { a.kp = 96; return encode_dispatch<8, 2>(a, xdt, cb, st); }
     a.kp = 192;
     return encode_dispatch<16, 1>(a, xdt, cb, st);
 }
 
 int launch_decode(const pkv_codec* c, const void* codes, int cb, int64_t n, int64_t cs,
-                  void* out, int odt, int64_t os, cudaStream_t st) {
+                  void* out, int odt, int64_t os, int64_t group_rows, int64_t group_stride, cudaStream_t st) {
     CodecArgs a{};
     fill_args(a, c);
     a.in = codes; a.out = out; a.n = n; a.in_stride = cs; a.out_stride = os;
+    a.group_rows = group_rows; a.group_stride = group_stride;
     if (a.m <= 32) { a.kp = 96; return decode_dispatch<8, 2>(a, cb, odt, st); }
     a.kp = 192;
     return decode_dispatch<16, 1>(a, cb, odt, st);

@@ -182,6 +182,48 @@ def dec_xy_polar(r_max: float, bits_r: int, bits_theta: int) -> np.ndarray:
     return np.stack([(r_q * c).astype(F32), (r_q * s).astype(F32)], axis=-1)
 
 
+CELL_GRID = 64          # cells per axis of the nearest-centroid candidate grid
+CELL_MAX = 16           # candidates kept per cell; fuller cells fall back to the full scan
+
+
+def centroid_cells(codebook: np.ndarray, half_width: float, grid: int = CELL_GRID, max_cand: int = CELL_MAX):
+    """Candidate centroids per cell of a grid over [-half_width, half_width]^2, per z-bin.
+
+    Centroid k is a candidate of cell Q when its least squared distance to Q is
+    within a rounding margin of min_j (greatest squared distance from Q to c_j):
+    for any point p of Q the nearest centroid (and every centroid whose fp32
+    distance could tie with it) satisfies that bound, so scanning the candidates
+    in index order gives the full scan's first-minimal index.  Cells are widened
+    by 1e-4 of their width to absorb the fp32 rounding of the point-to-cell map.
+    Returns (idx uint8 [Cz, grid, grid, max_cand], cnt uint8 [Cz, grid, grid]);
+    cnt 255 marks a cell with more than max_cand candidates.
+    """
+    cb = np.asarray(codebook, dtype=np.float64)
+    Cz, K, _ = cb.shape
+    if K > 256:
+        raise ValueError("candidate cells index at most 256 centroids")
+    w = 2.0 * half_width / grid
+    edges = -half_width + w * np.arange(grid + 1)
+    lo, hi = edges[:-1] - 1e-4 * w, edges[1:] + 1e-4 * w
+    idx = np.zeros((Cz, grid, grid, max_cand), dtype=np.uint8)
+    cnt = np.zeros((Cz, grid, grid), dtype=np.uint8)
+    for b in range(Cz):
+        cx, cy = cb[b, :, 0], cb[b, :, 1]
+        dxn = np.maximum(np.maximum(lo[:, None] - cx[None, :], 0.0), cx[None, :] - hi[:, None])
+        dxf = np.maximum(np.abs(lo[:, None] - cx[None, :]), np.abs(hi[:, None] - cx[None, :]))
+        dyn = np.maximum(np.maximum(lo[:, None] - cy[None, :], 0.0), cy[None, :] - hi[:, None])
+        dyf = np.maximum(np.abs(lo[:, None] - cy[None, :]), np.abs(hi[:, None] - cy[None, :]))
+        near = dyn[:, None, :] ** 2 + dxn[None, :, :] ** 2           # [y cell, x cell, k]
+        far = dyf[:, None, :] ** 2 + dxf[None, :, :] ** 2
+        bound = far.min(axis=2) * (1.0 + 1e-5) + 1e-6
+        cand = near <= bound[..., None]
+        n = cand.sum(axis=2)
+        cnt[b] = np.where(n > max_cand, 255, n).astype(np.uint8)
+        order = np.argsort(~cand, axis=2, kind="stable")[..., :max_cand]   # candidate indices first, ascending
+        idx[b] = np.where(np.arange(max_cand)[None, None, :] < n[..., None], order, 0).astype(np.uint8)
+    return idx, cnt
+
+
 @dataclass
 class HostTables:
     dim: int
@@ -200,6 +242,9 @@ class HostTables:
     dec_xy: np.ndarray
     bias_xy: Optional[np.ndarray] = None     # (C_z, 2) clamped BiasTable (x, y) terms
     z_uniform: bool = False                  # dec_z[i] = z_min + (i + 0.5) * delta_z (no Lloyd-Max, no bias)
+    cell_idx: Optional[np.ndarray] = None    # learned codebooks: candidate centroids per grid cell
+    cell_cnt: Optional[np.ndarray] = None
+    cell_half_width: float = 0.0
 
 
 def build_host_tables(dim: int, bits_z: int, bits_r: int, bits_theta: int, R: np.ndarray,
@@ -239,9 +284,13 @@ def build_host_tables(dim: int, bits_z: int, bits_r: int, bits_theta: int, R: np
         bias_xy = np.ascontiguousarray(b[:, 1:3])
     if not xy_per_z:
         xy = xy[0]
+    cells = (None, None)
+    if codebook is not None and K <= 256:
+        cells = centroid_cells(cb, float(r_max))
     return HostTables(dim=dim, bits=(bits_z, bits_r, bits_theta), xy_mode=xy_mode, xy_per_z=xy_per_z,
                       z_nan_bin=z_nan_bin, z_hi=float(z_hi), r_max=float(r_max),
                       R=np.ascontiguousarray(R, dtype=F32), z_thr=z_thr.astype(F32),
                       r2_thr=r2.astype(F32), th_thr=th.astype(F32), codebook=cb,
                       dec_z=dz.astype(F32), dec_xy=np.ascontiguousarray(xy, dtype=F32), bias_xy=bias_xy,
-                      z_uniform=(lloyd_boundaries is None and lloyd_centroids is None and bias_table is None))
+                      z_uniform=(lloyd_boundaries is None and lloyd_centroids is None and bias_table is None),
+                      cell_idx=cells[0], cell_cnt=cells[1], cell_half_width=float(r_max) if cells[0] is not None else 0.0)

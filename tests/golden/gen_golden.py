@@ -190,11 +190,70 @@ def scores_case(ref, name, B, H, Sq, Sk, d, bits, seed):
          bits=np.array(bits, np.int32))
 
 
+def raw_cache_case(ref):
+    """RawKVCache over one (batch, head) group, two updates, and a 2x3-group single update."""
+    from prismkv.cache.raw_cache import RawKVCache
+    be = ref["Backend"](ref["Config"](), head_dim=64)
+    g = torch.Generator().manual_seed(21)
+    k1, v1 = torch.randn(1, 1, 5, 64, generator=g), torch.randn(1, 1, 5, 64, generator=g)
+    k2, v2 = torch.randn(1, 1, 3, 64, generator=g), torch.randn(1, 1, 3, 64, generator=g)
+    cache = RawKVCache(be)
+    cache.update(0, k1, v1)
+    kf, vf = cache.update(0, k2, v2)
+    kc, vc = cache.get_codes(0)
+    k3, v3 = torch.randn(2, 3, 4, 64, generator=g), torch.randn(2, 3, 4, 64, generator=g)
+    kf3, vf3 = RawKVCache(be).update(1, k3, v3)
+    save("raw_cache_d64", k1=k1.numpy(), v1=v1.numpy(), k2=k2.numpy(), v2=v2.numpy(),
+         k_full=kf.numpy(), v_full=vf.numpy(), k_codes=kc.numpy(), v_codes=vc.numpy(),
+         seq_len=np.int32(cache.get_seq_length(0)), k3=k3.numpy(), v3=v3.numpy(),
+         k3_full=kf3.numpy(), v3_full=vf3.numpy(), **quant_state(be._quantizer))
+
+
+def kv_cache_case(ref):
+    """PrismKVCache (HF DynamicCache) over two updates, and the file its save_cache writes."""
+    from prismkv.cache.kv_cache import PrismKVCache
+    from prismkv.cache.cache_store import save_cache
+    g = torch.Generator().manual_seed(22)
+    k1, v1 = torch.randn(1, 2, 4, 96, generator=g), torch.randn(1, 2, 4, 96, generator=g)
+    k2, v2 = torch.randn(1, 2, 1, 96, generator=g), torch.randn(1, 2, 1, 96, generator=g)
+    cache = PrismKVCache(ref["Config"]())
+    cache.update(k1, v1, 0)
+    kf, vf = cache.update(k2, v2, 0)
+    save("kv_cache_d96", k1=k1.numpy(), v1=v1.numpy(), k2=k2.numpy(), v2=v2.numpy(),
+         k_full=kf.numpy(), v_full=vf.numpy(), **quant_state(cache._quantizers[0]))
+    one = PrismKVCache(ref["Config"]())
+    one.update(k1, v1, 0)
+    save_cache(one, os.path.join(HERE, "ref_cache_store.npz"))
+    print(f"ref_cache_store: {os.path.getsize(os.path.join(HERE, 'ref_cache_store.npz')) / 1024:.1f} KB")
+
+
+def vllm_block_case(ref):
+    """VLLMSwapCompressor block round trip: fp16 (heads, block, 64) -> int16 codes -> fp16."""
+    from prismkv.cache.vllm_adapter import VLLMSwapCompressor
+    comp = VLLMSwapCompressor(ref["Config"](), head_dim=64, n_layers=2)
+    g = torch.Generator().manual_seed(23)
+    kb = torch.randn(2, 16, 64, generator=g).half()
+    vb = torch.randn(2, 16, 64, generator=g).half()
+    kc, vc = comp.compress_block(1, 7, kb, vb)
+    kd, vd = comp.decompress_block(1, 7, 2, 16, dtype=torch.float16, device="cpu")
+    save("vllm_block_d64", k_block=kb.numpy(), v_block=vb.numpy(), k_codes=kc.numpy(), v_codes=vc.numpy(),
+         k_dec=kd.numpy(), v_dec=vd.numpy(), **quant_state(comp._backends[1]._quantizer))
+
+
+CASES = {"enc": None, "backend_d64": backend_case, "attn_v1": attn_v1_case, "attn_v2_gqa": attn_v2_gqa_case,
+         "raw_cache_d64": raw_cache_case, "kv_cache_d96": kv_cache_case, "vllm_block_d64": vllm_block_case}
+
+
 def main():
     if not any("reference" in p for p in sys.path + os.environ.get("PYTHONPATH", "").split(":")):
         print("set PYTHONPATH to the reference's src directory", file=sys.stderr)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = _ref()
+    only = sys.argv[1:]                      # case names to (re)generate; none = all
+    if only:
+        for name in only:
+            CASES[name](ref)
+        return
     enc_case(ref, "enc_v1_444", (4, 4, 4), 768, seed=0)
     enc_case(ref, "enc_v1_332", (3, 3, 2), 384, seed=1, scale_rows=True)
     enc_case(ref, "enc_v2_cb_bias", (4, 4, 4), 384, seed=2, codebook=True, bias=True)
@@ -207,6 +266,9 @@ def main():
     attn_v2_gqa_case(ref)
     scores_case(ref, "scores_d66", 1, 2, 4, 6, 66, (4, 4, 4), 42)
     scores_case(ref, "scores_d96_332", 2, 3, 3, 37, 96, (3, 3, 2), 5)
+    raw_cache_case(ref)
+    kv_cache_case(ref)
+    vllm_block_case(ref)
 
 
 if __name__ == "__main__":

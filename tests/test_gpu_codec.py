@@ -181,3 +181,85 @@ def test_reencode_of_decoded_is_idempotent_full_size(cuda_ready, variant):
         assert torch.equal(fold(c1[keep]), fold(c2[keep]))
     else:
         assert (c1 != c2).float().mean().item() < 1e-4      # duplicate-nearest centroids only
+
+
+@pytest.mark.parametrize("bits", [(4, 4, 4), (3, 3, 2)])
+def test_learned_encode_candidate_cells_equal_full_scan(cuda_ready, bits):
+    """The per-cell candidate lists give exactly the full 2^(br+bt)-centroid scan's indices:
+    points at all scales (inside, at the edge of and beyond the cell grid) and on cell edges."""
+    q = _quantizer("learned", bits)
+    codec = q.codec(torch.device(DEV))
+    assert codec.struct.cell_grid == 64
+    g = torch.Generator().manual_seed(77)
+    parts = [torch.randn(20000, 96, generator=g) * s for s in (0.3, 1.0, 3.0, 8.0)]
+    # rows whose rotated (x, y) land exactly on cell edges: rotate grid points back with R
+    edge = torch.zeros(4096, 96)
+    w = 2 * q.r_max / 64
+    vals = (torch.randint(-32, 33, (4096, 64), generator=g).float() * w).reshape(4096, 64)
+    rot = torch.zeros(4096, 96)
+    rot[:, 1::3] = vals[:, :32]
+    rot[:, 2::3] = vals[:, 32:]
+    edge = rot @ q.R
+    X = torch.cat(parts + [edge]).float().to(DEV)
+    with_cells = codec.encode(X).cpu()
+    saved = codec.struct.cell_grid
+    codec.struct.cell_grid = 0
+    try:
+        full = codec.encode(X).cpu()
+    finally:
+        codec.struct.cell_grid = saved
+    assert torch.equal(with_cells, full)
+
+
+def _force_cuda_core(codec):
+    """Context: the codec without its bf16 R parts, so encode takes the CUDA-core kernel."""
+    class _Ctx:
+        def __enter__(self):
+            self.saved = codec.struct.R_bf16x3
+            codec.struct.R_bf16x3 = None
+
+        def __exit__(self, *exc):
+            codec.struct.R_bf16x3 = self.saved
+    return _Ctx()
+
+
+@pytest.mark.parametrize("variant,bits", [("v1", (4, 4, 4)), ("v1", (3, 3, 2)), ("learned_bias", (4, 4, 4)),
+                                          ("lloyd", (4, 4, 4))])
+@pytest.mark.parametrize("n", [1, 127, 128, 129, 5000, 70001])
+def test_tensor_core_encode_matches_oracle(cuda_ready, variant, bits, n):
+    """bf16 rows of head_dim 96 are rotated on tcgen05 (R in three bf16 parts): codes equal the
+    oracle's except proven ties, and equal the CUDA-core kernel's except proven ties; every
+    partial tile and the grid-stride tail are covered by the sizes."""
+    q = _quantizer(variant, bits)
+    p = _params(q)
+    codec = q.codec(torch.device(DEV))
+    g = torch.Generator().manual_seed(n)
+    X = (torch.randn(n, 96, generator=g) * 1.3).to(torch.bfloat16)
+    Xd = X.to(DEV)
+    tc = codec.encode(Xd).cpu().numpy().astype(np.int64)
+    with _force_cuda_core(codec):
+        cc = codec.encode(Xd).cpu().numpy().astype(np.int64)
+    X32 = X.float().numpy()
+    rep = oracle.classify(X32, q.R.numpy(), p, tc, oracle.encode(X32, q.R.numpy(), p))
+    assert rep.unexplained == 0, rep.examples
+    assert rep.mismatches <= max(2, int(rep.total * TIE_RATE))
+    rep2 = oracle.classify(X32, q.R.numpy(), p, tc, cc)
+    assert rep2.unexplained == 0, rep2.examples
+
+
+def test_tensor_core_encode_strided_rows_and_cache_append(cuda_ready):
+    """Row stride > 96 (16-byte multiple) and the KV-cache append form (grouped code rows)."""
+    q = _quantizer("v1", (4, 4, 4))
+    codec = q.codec(torch.device(DEV))
+    g = torch.Generator(device=DEV).manual_seed(3)
+    big = torch.randn(3000, 128, generator=g, device=DEV).to(torch.bfloat16)
+    X = big[:, :96]
+    a = codec.encode(X)
+    b = codec.encode(X.contiguous())
+    assert torch.equal(a, b)
+    cache = torch.zeros(4, 1000, 32, dtype=torch.int16, device=DEV)
+    xs = torch.randn(4, 300, 96, generator=g, device=DEV).to(torch.bfloat16)
+    codec.encode_append(xs, cache, 77)
+    ref = codec.encode(xs.reshape(-1, 96)).view(4, 300, 32)
+    assert torch.equal(cache[:, 77:377], ref)
+    assert (cache[:, :77] == 0).all() and (cache[:, 377:] == 0).all()
