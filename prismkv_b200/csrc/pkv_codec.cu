@@ -117,8 +117,10 @@ __device__ __forceinline__ int nearest_centroid(const float2* __restrict__ cb, i
 // full scan's.  Points outside the grid or in an overfull cell scan all K.
 constexpr int kCellMax = 16;
 
+// cb: bin iz's centroids in global memory; cb_fast: the same centroids where
+// they are cheaper to read (a shared-memory copy), or cb itself.
 __device__ __forceinline__ int nearest_centroid_cells(const CodecArgs& a, int iz, const float2* __restrict__ cb,
-                                                      float x, float y) {
+                                                      const float2* cb_fast, float x, float y) {
     if (a.cell_grid > 0 && isfinite(x) && isfinite(y)) {
         const float fx = (x - a.cell_lo) * a.cell_scale, fy = (y - a.cell_lo) * a.cell_scale;
         if (fx >= 0.f && fy >= 0.f && fx < (float)a.cell_grid && fy < (float)a.cell_grid) {
@@ -130,7 +132,7 @@ __device__ __forceinline__ int nearest_centroid_cells(const CodecArgs& a, int iz
                 int bi = 0;
                 for (int i = 0; i < n; ++i) {
                     const int k = __ldg(cand + i);
-                    const float2 c = __ldg(cb + k);
+                    const float2 c = cb_fast[k];
                     const float dx = x - c.x, dy = y - c.y;
                     const float d2 = fmaf(dx, dx, dy * dy);
                     if (d2 < best) { best = d2; bi = k; }
@@ -146,8 +148,9 @@ __device__ __forceinline__ int nearest_centroid_cells(const CodecArgs& a, int iz
 // values >= z_hi as the reference's chain maps them), then the uniform polar
 // bins (r^2 and atan2 thresholds) or the nearest learned centroid of bin i_z.
 // thr: z | r^2 | theta thresholds, nz = 2^bits_z - 1, nr = 2^bits_r - 1.
+// cb_smem: the whole codebook in shared memory, or nullptr.
 __device__ __forceinline__ uint32_t encode_triplet(const CodecArgs& a, const float* thr, int nz, int nr, float z,
-                                                   float xx, float yy) {
+                                                   float xx, float yy, const float2* cb_smem = nullptr) {
     int iz;
     if (isnan(z)) iz = a.z_nan_bin;
     else if (z >= a.z_hi) iz = 0;
@@ -160,7 +163,7 @@ __device__ __forceinline__ uint32_t encode_triplet(const CodecArgs& a, const flo
         flat = ((uint32_t)ir << a.bits_t) | (uint32_t)it;
     } else {
         const float2* cb = reinterpret_cast<const float2*>(a.codebook) + (size_t)iz * a.K;
-        flat = (uint32_t)nearest_centroid_cells(a, iz, cb, xx, yy);
+        flat = (uint32_t)nearest_centroid_cells(a, iz, cb, cb_smem ? cb_smem + (size_t)iz * a.K : cb, xx, yy);
     }
     return ((uint32_t)iz << a.bits_flat) | flat;
 }

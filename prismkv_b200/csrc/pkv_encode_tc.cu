@@ -16,8 +16,9 @@
 //              swizzle) into a 4-stage ring; the R parts once.
 //   warp 1     owns the tensor memory (256 columns = two accumulators) and
 //              one lane issues the 18 MMAs of a tile (3 parts x 6 K-steps).
-//   warps 2-9  epilogue: each TMEM lane quarter is read by two warps, one per
-//              half of the 32 triplets; tcgen05.ld -> bins -> packed codes.
+//   warps 2-17 epilogue: each TMEM lane quarter is read by four warps, one per
+//              quarter of the 32 triplets; tcgen05.ld -> bins -> 8 packed codes
+//              per thread, written with one vector store.
 // Every mbarrier wait is bounded; on expiry the kernel sets the device error
 // word, drains what it issued and frees its tensor memory before returning.
 
@@ -39,11 +40,14 @@ constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_TILE;
 constexpr int OFF_THR = OFF_B + NPART * B_PART;
 constexpr int THR_FLOATS = 3 * 255;
-constexpr int OFF_BAR = OFF_THR + THR_FLOATS * 4 + 4;       // 8-byte aligned below
+constexpr int OFF_CB = OFF_THR + THR_FLOATS * 4 + 4;        // learned codebook copy (16-byte aligned below)
+constexpr int CB_BYTES = 32 * 1024;                         // up to 16 z-bins x 256 centroids
+constexpr int OFF_BAR = OFF_CB + 16 + CB_BYTES;             // 8-byte aligned below
 constexpr int NBAR = 2 * STAGES + 1 + 2 + 2;                // full, empty, bfull, acc_full[2], acc_empty[2]
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8 + 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;            // + alignment slack of the 1024-byte base
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 16;
+constexpr int TRI = 8;                     // triplets per epilogue thread
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
 constexpr int TMEM_COLS = 256;
 // instruction descriptor: D f32 (bits 4-5 = 1), A bf16 (7-9 = 1), B bf16 (10-12 = 1), both K-major,
@@ -80,6 +84,16 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
+// 8 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    #pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // 16 consecutive fp32 columns of this thread's TMEM lane
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
@@ -109,6 +123,7 @@ encode_tc_kernel(CodecArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
     uint64_t* acc_full = bfull + 1;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+    float2* cb_s = reinterpret_cast<float2*>(smem + ((OFF_CB + 15) & ~15));
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nz = (1 << a.bits_z) - 1, nr = (1 << a.bits_r) - 1, nt = (1 << a.bits_t) - 1;
@@ -116,6 +131,11 @@ encode_tc_kernel(CodecArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
     if (a.xy_mode == 0) {
         for (int i = tid; i < nr; i += THREADS) thr[nz + i] = __ldg(a.r2_thr + i);
         for (int i = tid; i < nt; i += THREADS) thr[nz + nr + i] = __ldg(a.th_thr + i);
+    }
+    const bool cb_in_smem = a.xy_mode == 1 && (int64_t)(nz + 1) * a.K * 8 <= CB_BYTES;
+    if (cb_in_smem) {
+        const float2* g = reinterpret_cast<const float2*>(a.codebook);
+        for (int i = tid; i < (nz + 1) * a.K; i += THREADS) cb_s[i] = __ldg(g + i);
     }
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -196,31 +216,50 @@ encode_tc_kernel(CodecArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
         }
     } else {
         // ---------------- epilogue ----------------
-        const int quarter = warp & 3, half = (warp - 2) >> 2;
+        const int quarter = warp & 3, slice = (warp - 2) >> 2;      // TMEM lane quarter, 8-triplet slice
         const int row = quarter * 32 + lane;
-        using CT = typename Code<CB>::T;
-        CT* codes = static_cast<CT*>(a.out);
         int it = 0;
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
             const int b = it & 1;
             // warp-uniform: tcgen05.ld below is .sync.aligned, so all lanes go on or none does
             if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (it >> 1) & 1, kErrWaitFull))) break;
             tc_fence_after();
-            float v[48];
-            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 128 + half * 48);
+            float v[3 * TRI];
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 128 + slice * 3 * TRI);
             tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(v));
-            tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-            tmem_ld16(taddr + 32, *reinterpret_cast<float(*)[16]>(v + 32));
+            tmem_ld8(taddr + 16, v + 16);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
             const int64_t n = t * BM + row;
             if (n < a.n) {
-                CT* crow = codes + code_row(a, n, a.out_stride) + 16 * half;
+                uint32_t c[TRI];
                 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    Code<CB>::store(crow + j, encode_triplet(a, thr, nz, nr, v[3 * j], v[3 * j + 1], v[3 * j + 2]));
+                for (int j = 0; j < TRI; ++j)
+                    c[j] = encode_triplet(a, thr, nz, nr, v[3 * j], v[3 * j + 1], v[3 * j + 2],
+                                          cb_in_smem ? cb_s : nullptr);
+                if (CB == 2) {
+                    uint16_t* dst = static_cast<uint16_t*>(a.out) + code_row(a, n, a.out_stride) + TRI * slice;
+                    const uint4 w = make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16),
+                                               c[6] | (c[7] << 16));
+                    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                        *reinterpret_cast<uint4*>(dst) = w;
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < TRI; ++j) dst[j] = (uint16_t)c[j];
+                    }
+                } else {
+                    uint8_t* dst = static_cast<uint8_t*>(a.out) + code_row(a, n, a.out_stride) + TRI * slice;
+                    const uint2 w = make_uint2(c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24),
+                                               c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24));
+                    if ((reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+                        *reinterpret_cast<uint2*>(dst) = w;
+                    } else {
+                        #pragma unroll
+                        for (int j = 0; j < TRI; ++j) dst[j] = (uint8_t)c[j];
+                    }
+                }
             }
         }
     }
