@@ -27,6 +27,31 @@ def code_dtype_for(bits_total: int) -> torch.dtype:
     return torch.uint8 if bits_total <= 8 else torch.int16
 
 
+def split_bf16x3(R: np.ndarray) -> np.ndarray:
+    """R (fp32) as three bf16 parts, returned as their uint16 bit patterns (3, *R.shape).
+
+    R1 and R2 truncate toward zero and R3 rounds to nearest, so every part has
+    the sign of R and R1 + R2 + R3 equals R to within 2^-24 |R|.  A part that
+    comes out exactly zero for a non-zero entry becomes the smallest bf16
+    normal (2^-126) with R's sign: an infinite input then meets no zero and no
+    opposite-signed part, and rotates to the same +-inf (or NaN) as an fp32
+    dot product, while finite results move by less than 2^-126 |x|.
+    """
+    r = np.ascontiguousarray(R, dtype=np.float32)
+    bits = r.view(np.uint32)
+    r1 = (bits & 0xFFFF0000).view(np.float32)
+    rem = (r - r1).astype(np.float32)
+    r2 = (rem.view(np.uint32) & 0xFFFF0000).view(np.float32)
+    rem2 = (r - r1 - r2).astype(np.float32)
+    r3 = torch.from_numpy(rem2).to(torch.bfloat16).float().numpy()       # round to nearest even
+    parts = []
+    tiny = np.where(np.signbit(r), np.float32(-2.0 ** -126), np.float32(2.0 ** -126)).astype(np.float32)
+    for part in (r1, r2, r3):
+        part = np.where((part == 0) & (r != 0), tiny, part).astype(np.float32)
+        parts.append((part.view(np.uint32) >> 16).astype(np.uint16))
+    return np.stack(parts)
+
+
 class DeviceCodec:
     def __init__(self, host: HostTables, device: torch.device):
         self.host = host
@@ -43,12 +68,7 @@ class DeviceCodec:
             return torch.from_numpy(a).to(self.device)
 
         self._R = up(host.R)
-        # R as three bf16 parts for the tensor-core rotation (exact products, fp32 accumulation)
-        r = torch.from_numpy(np.ascontiguousarray(host.R, dtype=np.float32))
-        r1 = r.to(torch.bfloat16)
-        r2 = (r - r1.float()).to(torch.bfloat16)
-        r3 = (r - r1.float() - r2.float()).to(torch.bfloat16)
-        self._R_bf16x3 = torch.stack([r1, r2, r3]).contiguous().to(self.device)
+        self._R_bf16x3 = torch.from_numpy(split_bf16x3(host.R)).view(torch.bfloat16).to(self.device)
         self._z_thr = up(host.z_thr)
         self._r2 = up(host.r2_thr)
         self._th = up(host.th_thr)

@@ -148,18 +148,50 @@ __device__ __forceinline__ int nearest_centroid_cells(const CodecArgs& a, int iz
 // values >= z_hi as the reference's chain maps them), then the uniform polar
 // bins (r^2 and atan2 thresholds) or the nearest learned centroid of bin i_z.
 // thr: z | r^2 | theta thresholds, nz = 2^bits_z - 1, nr = 2^bits_r - 1.
-// cb_smem: the whole codebook in shared memory, or nullptr.
+// cb_smem: the whole codebook in shared memory, or nullptr.  g (optional):
+// linear first guesses of the three threshold counts (BinGuess), which replace
+// the binary searches by one or two comparisons.
+struct BinGuess {
+    float z0, zi, r0, ri, t0, ti;          // count ~ floor((f(v) - x0) * xi) + 1, f = sqrt for r^2
+};
+
+__device__ __forceinline__ BinGuess make_guess(const float* thr, int nz, int nr, int nt) {
+    auto lin = [](const float* t, int n, bool root, float& x0, float& xi) {
+        const float lo = root ? sqrtf(t[0]) : t[0], hi = root ? sqrtf(t[n - 1]) : t[n - 1];
+        x0 = lo;
+        xi = (n > 1 && hi > lo) ? (float)(n - 1) / (hi - lo) : 0.f;
+    };
+    BinGuess g;
+    lin(thr, nz, false, g.z0, g.zi);
+    lin(thr + nz, nr, true, g.r0, g.ri);
+    lin(thr + nz + nr, nt, false, g.t0, g.ti);
+    return g;
+}
+
+__device__ __forceinline__ int guess_count(float v, float x0, float xi) {
+    return __float2int_rd(fmaf(v - x0, xi, 1.f));  // saturating (no overflow at +-inf); NaN gives 0
+}
+
 __device__ __forceinline__ uint32_t encode_triplet(const CodecArgs& a, const float* thr, int nz, int nr, float z,
-                                                   float xx, float yy, const float2* cb_smem = nullptr) {
+                                                   float xx, float yy, const float2* cb_smem = nullptr,
+                                                   const BinGuess* g = nullptr) {
     int iz;
     if (isnan(z)) iz = a.z_nan_bin;
     else if (z >= a.z_hi) iz = 0;
-    else iz = count_ge(thr, a.bits_z, z);
+    else iz = g ? count_ge_from(thr, nz, z, guess_count(z, g->z0, g->zi)) : count_ge(thr, a.bits_z, z);
     uint32_t flat;
     if (a.xy_mode == 0) {
         float s = __fadd_rn(__fmul_rn(xx, xx), __fmul_rn(yy, yy));
-        int ir = count_ge(thr + nz, a.bits_r, s);
-        int it = count_ge(thr + nz + nr, a.bits_t, atan2f(yy, xx));
+        const float th = atan2f(yy, xx);
+        const int nt = (1 << a.bits_t) - 1;
+        int ir, it;
+        if (g) {
+            ir = count_ge_from(thr + nz, nr, s, guess_count(sqrtf(s), g->r0, g->ri));
+            it = count_ge_from(thr + nz + nr, nt, th, guess_count(th, g->t0, g->ti));
+        } else {
+            ir = count_ge(thr + nz, a.bits_r, s);
+            it = count_ge(thr + nz + nr, a.bits_t, th);
+        }
         flat = ((uint32_t)ir << a.bits_t) | (uint32_t)it;
     } else {
         const float2* cb = reinterpret_cast<const float2*>(a.codebook) + (size_t)iz * a.K;

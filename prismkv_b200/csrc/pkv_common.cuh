@@ -71,6 +71,19 @@ __device__ __forceinline__ int count_ge(const float* t, int bits, float v) {
     return lo;
 }
 
+// The same count from a first guess: `guess` is any integer (a linear
+// interpolation of the thresholds is exact up to one step for uniform bins);
+// the loops move it to the unique g with t[g-1] <= v < t[g].  NaN yields 0.
+__device__ __forceinline__ int count_ge_from(const float* t, int n, float v, int guess) {
+    int g = min(max(guess, 0), n);
+    if (g > 0 && !(v >= t[g - 1])) {
+        do { --g; } while (g > 0 && !(v >= t[g - 1]));
+    } else {
+        while (g < n && v >= t[g]) ++g;
+    }
+    return g;
+}
+
 // ---------------------------------------------------------------------------
 // mbarrier / bulk-copy PTX (sm_90+), with bounded waits
 // ---------------------------------------------------------------------------

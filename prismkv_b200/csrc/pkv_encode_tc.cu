@@ -133,6 +133,7 @@ encode_tc_kernel(CodecArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
         for (int i = tid; i < nt; i += THREADS) thr[nz + nr + i] = __ldg(a.th_thr + i);
     }
     const bool cb_in_smem = a.xy_mode == 1 && (int64_t)(nz + 1) * a.K * 8 <= CB_BYTES;
+    __syncthreads();                        // thresholds in place for the guesses below
     if (cb_in_smem) {
         const float2* g = reinterpret_cast<const float2*>(a.codebook);
         for (int i = tid; i < (nz + 1) * a.K; i += THREADS) cb_s[i] = __ldg(g + i);
@@ -217,6 +218,7 @@ encode_tc_kernel(CodecArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
     } else {
         // ---------------- epilogue ----------------
         const int quarter = warp & 3, slice = (warp - 2) >> 2;      // TMEM lane quarter, 8-triplet slice
+        const BinGuess guess = make_guess(thr, nz, nr, nt);
         const int row = quarter * 32 + lane;
         int it = 0;
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
@@ -238,7 +240,7 @@ encode_tc_kernel(CodecArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
                 #pragma unroll
                 for (int j = 0; j < TRI; ++j)
                     c[j] = encode_triplet(a, thr, nz, nr, v[3 * j], v[3 * j + 1], v[3 * j + 2],
-                                          cb_in_smem ? cb_s : nullptr);
+                                          cb_in_smem ? cb_s : nullptr, &guess);
                 if (CB == 2) {
                     uint16_t* dst = static_cast<uint16_t*>(a.out) + code_row(a, n, a.out_stride) + TRI * slice;
                     const uint4 w = make_uint4(c[0] | (c[1] << 16), c[2] | (c[3] << 16), c[4] | (c[5] << 16),

@@ -263,3 +263,23 @@ def test_tensor_core_encode_strided_rows_and_cache_append(cuda_ready):
     ref = codec.encode(xs.reshape(-1, 96)).view(4, 300, 32)
     assert torch.equal(cache[:, 77:377], ref)
     assert (cache[:, :77] == 0).all() and (cache[:, 377:] == 0).all()
+
+
+def test_tensor_core_encode_edge_rows(cuda_ready):
+    """Edge rows through the tensor-core epilogue (first-guess bin counts): zeros, huge,
+    tiny, +-inf and NaN components, in bf16, against the CUDA-core kernel."""
+    for variant in ("v1", "lloyd", "learned"):
+        q = _quantizer(variant, (4, 4, 4))
+        codec = q.codec(torch.device(DEV))
+        g = torch.Generator().manual_seed(9)
+        rows = [torch.zeros(96), torch.randn(96, generator=g) * 1e30, torch.randn(96, generator=g) * 1e-30,
+                torch.randn(96, generator=g) * 60]
+        for k, val in ((3, float("inf")), (10, float("nan")), (0, -float("inf")), (40, float("inf"))):
+            r = torch.randn(96, generator=g)
+            r[k] = val
+            rows.append(r)
+        X = torch.stack(rows * 40).to(torch.bfloat16).to(DEV)
+        tc = codec.encode(X)
+        with _force_cuda_core(codec):
+            cc = codec.encode(X)
+        assert torch.equal(tc, cc), variant

@@ -114,3 +114,18 @@ def test_decode_tables_match_reference_dequant(variant):
     tol = 2.0 ** -21 * p.r_max
     np.testing.assert_allclose(xy[:, 0], ref[:, 1], atol=tol, rtol=0)
     np.testing.assert_allclose(xy[:, 1], ref[:, 2], atol=tol, rtol=0)
+
+
+def test_split_bf16x3_exact_and_sign_preserving():
+    """R = R1 + R2 + R3 in bf16 parts: sum within 2^-24 |R|, every part with R's sign and
+    non-zero, so an infinite input component never meets inf - inf or inf * 0."""
+    from prismkv_b200.codec import split_bf16x3
+    from prismkv_b200.utils import make_rotation
+    for dim, seed in ((96, 42), (66, 7)):
+        R = make_rotation(dim, seed).numpy()
+        parts = (split_bf16x3(R).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+        err = np.abs(parts.sum(0) - R.astype(np.float64))
+        assert (err <= 2.0 ** -24 * np.abs(R)).all()
+        assert (np.sign(parts) == np.sign(R)[None]).all() and (parts != 0).all()
+    z = split_bf16x3(np.array([[0.0, 1.0, -3.0]], np.float32))
+    assert (z[:, 0, 0] == 0).all()                      # an exact zero stays zero
