@@ -176,9 +176,16 @@ __device__ __forceinline__ uint32_t encode_triplet(const CodecArgs& a, const flo
                                                    float xx, float yy, const float2* cb_smem = nullptr,
                                                    const BinGuess* g = nullptr) {
     int iz;
-    if (isnan(z)) iz = a.z_nan_bin;
-    else if (z >= a.z_hi) iz = 0;
-    else iz = g ? count_ge_from(thr, nz, z, guess_count(z, g->z0, g->zi)) : count_ge(thr, a.bits_z, z);
+    if (g) {
+        // uniform z bins: the linear guess is within one bin; Lloyd-Max (z_hi NaN): binary search
+        const int c = isnan(a.z_hi) ? count_ge_unrolled(thr, a.bits_z, z)
+                                    : count_ge_window(thr, nz, z, guess_count(z, g->z0, g->zi));
+        iz = isnan(z) ? a.z_nan_bin : (z >= a.z_hi ? 0 : c);
+    } else {
+        if (isnan(z)) iz = a.z_nan_bin;
+        else if (z >= a.z_hi) iz = 0;
+        else iz = count_ge(thr, a.bits_z, z);
+    }
     uint32_t flat;
     if (a.xy_mode == 0) {
         float s = __fadd_rn(__fmul_rn(xx, xx), __fmul_rn(yy, yy));
@@ -186,8 +193,8 @@ __device__ __forceinline__ uint32_t encode_triplet(const CodecArgs& a, const flo
         const int nt = (1 << a.bits_t) - 1;
         int ir, it;
         if (g) {
-            ir = count_ge_from(thr + nz, nr, s, guess_count(sqrtf(s), g->r0, g->ri));
-            it = count_ge_from(thr + nz + nr, nt, th, guess_count(th, g->t0, g->ti));
+            ir = count_ge_window(thr + nz, nr, s, guess_count(sqrtf(s), g->r0, g->ri));
+            it = count_ge_window(thr + nz + nr, nt, th, guess_count(th, g->t0, g->ti));
         } else {
             ir = count_ge(thr + nz, a.bits_r, s);
             it = count_ge(thr + nz + nr, a.bits_t, th);

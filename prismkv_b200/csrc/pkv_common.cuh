@@ -71,6 +71,36 @@ __device__ __forceinline__ int count_ge(const float* t, int bits, float v) {
     return lo;
 }
 
+// The same count, branch-free, when the true count lies within 2 of `guess`:
+// every threshold below the window counts and none above it does, so the count
+// is the window's base plus its four comparisons.  NaN yields 0 (all compares
+// false, and a NaN guess is 0).
+__device__ __forceinline__ int count_ge_window(const float* t, int n, float v, int guess) {
+    const int base = min(max(guess - 2, 0), n);
+    int c = base;
+    #pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int b = base + i;
+        const float tb = t[min(b, n - 1)];
+        c += (b < n && v >= tb) ? 1 : 0;
+    }
+    return c;
+}
+
+// Binary-search count with a fixed, unrolled step count (bits <= 8), predicated
+// rather than branched, so independent searches interleave.
+__device__ __forceinline__ int count_ge_unrolled(const float* t, int bits, float v) {
+    int lo = 0;
+    #pragma unroll
+    for (int k = 7; k >= 0; --k) {
+        if (k < bits) {
+            const int probe = lo + (1 << k);
+            lo = (v >= t[probe - 1]) ? probe : lo;
+        }
+    }
+    return lo;
+}
+
 // The same count from a first guess: `guess` is any integer (a linear
 // interpolation of the thresholds is exact up to one step for uniform bins);
 // the loops move it to the unique g with t[g-1] <= v < t[g].  NaN yields 0.
