@@ -348,6 +348,7 @@ def bench_decode(args, ws, rank, device):
 def bench_encode(args, ws, rank, device):
     """Encode of one layer's new tokens: 32768 tokens x kv heads, K and V, bf16 in -> packed codes
     (learned-gqa: learned codebooks + BiasTable, 8 KV heads; phi3-decode: uniform polar, 32 heads)."""
+    import numpy as np
     from prismkv_b200 import _lib
     from prismkv_b200.synthetic import WORKLOADS, make_encode_input, make_quantizer
 
@@ -378,17 +379,65 @@ def bench_encode(args, ws, rank, device):
     assert _lib.device_error() == 0
     nbytes = x.numel() * x.element_size() + codes.numel() * 2
     peak, peak_kind = _peaks()
-    return {
+    kernel = "encode_tc_kernel" if (w.dim == 96 and x.dtype == torch.bfloat16) else "encode_kernel"
+
+    # end to end through the public API: pinned bf16 rows -> device -> encode -> codes back to the host
+    h_x = x.cpu().pin_memory()
+    h_codes = torch.empty(codes.shape, dtype=codes.dtype).pin_memory()
+    d_x = torch.empty_like(x)
+
+    def e2e_step():
+        d_x.copy_(h_x, non_blocking=True)
+        h_codes.copy_(quant.encode_compact(d_x), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(3, min(args.steps, 20))
+    e0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1) / n_e2e, ws, device)
+    line = {
         "metric": METRIC, "value": round(tokens * ws / (ms * 1e-3) / 1e6, 3), "unit": "Mtok/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, f32 rotation", "data": "synthetic",
         "config": {"workload": f"{w.name}-encode", "tokens": tokens, "kv_heads": w.kv_heads, "head_dim": w.dim,
-                   "input": "bf16", "codes": "uint16", "bytes_per_step": nbytes},
+                   "input": "bf16", "codes": "uint16", "bytes_per_step": nbytes, "l2": L2Scrub.DESCRIPTION},
         "roofline": {"bound": "hbm", "achieved": round(nbytes / (local_ms * 1e-3) / 1e9, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(nbytes / (local_ms * 1e-3) / 1e9 / peak, 4), "peak_kind": peak_kind,
-                     "traffic": _committed_traffic("encode_kernel", w.name), "kernel": "pkv::encode_kernel"},
+                     "traffic": _committed_traffic(kernel, w.name), "kernel": kernel},
+        "e2e": {"value": round(tokens * ws / (e2e_ms * 1e-3) / 1e6, 3), "unit": "Mtok/s",
+                "h2d_bytes_per_step": h_x.numel() * h_x.element_size(),
+                "d2h_bytes_per_step": h_codes.numel() * h_codes.element_size(), "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": args.steps, "clocks": clk.summary(),
     }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        import oracle
+        p = oracle.QuantParams.default(w.dim, *w.bits)
+        host = quant.codec(device).host
+        if host.xy_mode == 1:
+            p.codebook = host.codebook
+        rows = 2 * w.kv_heads * 256                      # 256 tokens of the layer, K and V of every head
+        xs = x[:rows].float().cpu().numpy()
+        R = quant.R.numpy()
+        oracle.encode(xs[:64], R, p)
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            oracle.encode(xs, R, p)
+            reps += 1
+            if time.perf_counter() - t0 > 10.0 or reps >= 20:
+                break
+        per = (time.perf_counter() - t0) / reps
+        line["cpu_baseline"] = {"value": round(256 / per / 1e6, 5), "unit": "Mtok/s", "cores": os.cpu_count(),
+                                "kind": "port", "sample": f"{rows} rows (256 tokens x {w.kv_heads} heads x K, V), "
+                                f"{reps} reps, {per * 1e3:.1f} ms each; NumPy restatement of "
+                                "StackedPlaneQuantizer.encode"}
+    return line
 
 
 def bench_reference(args, ws, rank):
