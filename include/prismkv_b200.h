@@ -203,9 +203,11 @@ PKV_API int pkv_attn_describe(const pkv_codec *c, const pkv_attn_args *a, pkv_at
  * decode path (a C/C++ host without a caching allocator, where cudaMalloc
  * would synchronise the device every step).  It has no counterpart in the
  * reference.  Limits: the partials, batch * q_heads * splits * (dim + 2)
- * floats rounded up to 256 bytes, must fit in 8 MiB - 64 KiB, and
- * batch * kv_heads must not exceed PKV_NOALLOC_MAX_KV_ROWS when the call
- * splits; otherwise PKV_ERR_SCRATCH_LIMIT and nothing is launched.  The first
+ * floats rounded up to 256 bytes, must fit in 8 MiB - 64 KiB, and the
+ * split's arrival counters -- batch * kv_heads, or batch * q_heads when
+ * grouped heads of 12-bit codes run one query head per unit -- must not
+ * exceed PKV_NOALLOC_MAX_KV_ROWS; otherwise PKV_ERR_SCRATCH_LIMIT and
+ * nothing is launched.  The first
  * call on a device resolves the array's address (cudaGetSymbolAddress, with
  * that device current) and zeroes its counter region on `stream`; make it
  * before any stream capture.  The counters must be zero when a kernel starts;

@@ -70,7 +70,7 @@ const char* pkv_strerror(int status) {
         case PKV_ERR_DEVICE: return "device-side error flag set (a bounded wait expired)";
         case PKV_ERR_SCRATCH_LIMIT:
             return "arguments need more split scratch than the static array of pkv_attn_decode_noalloc holds "
-                   "(8 MiB - 64 KiB of partials, 16384 batch x kv-head rows); use pkv_attn_decode with a workspace";
+                   "(8 MiB - 64 KiB of partials, 16384 split counters); use pkv_attn_decode with a workspace";
     }
     return "unknown status";
 }

@@ -63,6 +63,9 @@ struct AttnParams {
     // unit and at CTA boundaries.  slots: partial rows kept per (b, q head) in the workspace.
     int bal, tt, tpu, seg_cap, slots;
     int64_t tiles;
+    // Hu: work units per batch row -- Hkv, or Hq when every query head is its own unit reading
+    // KV head hq / Gq (grouped heads through a one-head kernel; the group's re-reads hit L2)
+    int Hu, Gq;
 };
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -75,15 +78,16 @@ __device__ __forceinline__ float q_load(const void* q, int qdt, int64_t idx) {
 
 // One segment of work: tokens [tok0, tok1) of (b, kv head hk).  The unit's
 // segments number nseg; this one writes partial slot `split` when nseg > 1.
-struct ItemRange { int b, hk, split, tok0, tok1, nseg; };
+struct ItemRange { int b, hk, split, tok0, tok1, nseg, kvh; };   // hk: unit head, kvh: its KV head
 
 __device__ __forceinline__ ItemRange item_range(const AttnParams& p, int item) {
     ItemRange r;
     r.nseg = p.nsplit;
     r.split = item % p.nsplit;
     int bh = item / p.nsplit;
-    r.hk = bh % p.Hkv;
-    r.b = bh / p.Hkv;
+    r.hk = bh % p.Hu;
+    r.b = bh / p.Hu;
+    r.kvh = r.hk / p.Gq;
     int L = p.seq_lens ? min(max(p.seq_lens[r.b], 0), p.S) : p.S;
     r.tok0 = r.split * p.chunk;
     r.tok1 = min(L, r.tok0 + p.chunk);
@@ -134,8 +138,9 @@ __device__ inline bool work_next(const AttnParams& p, WorkCursor& c, ItemRange& 
     const int64_t u = c.t / p.tpu, a = u * p.tpu, b = a + p.tpu;
     const int64_t cb = a + ((c.t - a) / p.seg_cap + 1) * p.seg_cap;
     const int64_t e = min(c.t_end, min(b, cb));
-    r.hk = (int)(u % p.Hkv);
-    r.b = (int)(u / p.Hkv);
+    r.hk = (int)(u % p.Hu);
+    r.b = (int)(u / p.Hu);
+    r.kvh = r.hk / p.Gq;
     r.tok0 = (int)(c.t - a) * p.tt;
     r.tok1 = min(p.S, (int)(e - a) * p.tt);
     balanced_slot(p, a, b, c.t, gridDim.x, r.split, r.nseg);
@@ -242,7 +247,7 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
         __threadfence();
         named_bar_sync(1, nthr);
         if (tid == 0) {
-            int32_t* cnt = p.ws_count + (r.b * p.Hkv + r.hk);
+            int32_t* cnt = p.ws_count + (r.b * p.Hu + r.hk);
             const int prev = atomicAdd(cnt, 1);
             const int last = (prev == r.nseg - 1);
             if (last) { __threadfence(); atomicExch(cnt, 0); }
@@ -342,7 +347,7 @@ __device__ void produce(const AttnParams& p, uint8_t* stage_base, int stage_byte
     WorkCursor wc = work_begin(p);
     ItemRange r;
     while (ok && work_next<BAL>(p, wc, r)) {
-        const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.hk * p.kv_hs) * code_bytes;
+        const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.kvh * p.kv_hs) * code_bytes;
         for (int pass = 0; pass < (KV_TOGETHER ? 1 : 2) && ok; ++pass) {
             for (int t0 = r.tok0; t0 < r.tok1; t0 += TT, ++seq) {
                 const int s = seq % p.stages;
@@ -1096,7 +1101,7 @@ __global__ void __launch_bounds__(TMA ? kLW * 32 + 32 : kLW * 32) attn_lut_kerne
             for (int tp = 0; tp < TPL; ++tp) acc[g][tp][0] = acc[g][tp][1] = acc[g][tp][2] = 0.f;
         }
         float lrun = 0.f;
-        const int64_t base = (int64_t)r.b * p.kv_bs + (int64_t)r.hk * p.kv_hs;
+        const int64_t base = (int64_t)r.b * p.kv_bs + (int64_t)r.kvh * p.kv_hs;
 
         for (int t0 = r.tok0; t0 < r.tok1; t0 += kLTT, ++seq) {
             const int s = seq % p.stages;
@@ -1290,6 +1295,7 @@ struct AttnPlan {
     int G, TPL, stages, nsplit, chunk, tt, threads, smem, ctas_per_sm;
     bool tma;
     bool bal;                          // balanced tile ranges instead of round-robin items
+    bool qunits;                       // one unit per query head (grouped heads in the one-head kernel)
     int tpu, seg_cap, slots;           // tiles per unit, tiles per segment at most, partial slots
     int64_t tiles, grid;               // balanced: total tiles, CTAs
 };
@@ -1310,8 +1316,11 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     pl.polar = pl.tma && m <= 32 && c->xy_mode == 0 && c->bits_z <= 4 && (c->bits_r + c->bits_theta) <= 8 &&
                (c->xy_per_z == 0 || c->bias_xy != nullptr);
     pl.mha12 = pl.polar && c->dim == 96 && a->code_bytes == 2 && c->bits_z == 4 && c->bits_r == 4 &&
-               c->bits_theta == 4 && pl.G == 1 && a->q_heads == a->kv_heads && c->xy_per_z == 0 &&
-               (c->flags & PKV_CODEC_Z_UNIFORM) != 0;
+               c->bits_theta == 4 && c->xy_per_z == 0 && (c->flags & PKV_CODEC_Z_UNIFORM) != 0;
+    // grouped heads: every query head streams its KV head's codes on its own (the group's re-reads
+    // of the same codes hit L2), which beats per-token work for the whole group at 12-bit codes
+    pl.qunits = pl.mha12 && a->q_heads != a->kv_heads;
+    if (pl.mha12) pl.G = 1;
     if (pl.mha12) {
         pl.TPL = 1;
         pl.tt = mha12::TT;
@@ -1347,7 +1356,7 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     // split count: minimise rounds * (tiles per item + overhead); items carry at most `chunk` tokens
     const int tiles_total = std::max(1, (a->seq_len + pl.tt - 1) / pl.tt);
     const int max_tiles_item = std::max(1, pl.chunk / pl.tt);
-    const int64_t units = (int64_t)a->batch * a->kv_heads;
+    const int64_t units = (int64_t)a->batch * (pl.qunits ? a->q_heads : a->kv_heads);
     const int64_t grid = (int64_t)num_sms() * pl.ctas_per_sm;
     int best = 0;
     double best_cost = 1e300;
@@ -1403,12 +1412,18 @@ void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* ou
     out->ctas_per_sm = pl.ctas_per_sm;
 }
 
+// Arrival counters of a split call: one per (batch row, unit head).
+size_t attn_counter_bytes(const pkv_codec* c, const pkv_attn_args* a) {
+    const AttnPlan pl = plan_attn(c, a);
+    return (size_t)a->batch * (pl.qunits ? a->q_heads : a->kv_heads) * sizeof(int32_t);
+}
+
 size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a) {
     AttnPlan pl = plan_attn(c, a);
     if (!pl.bal && pl.nsplit <= 1) return 0;
     size_t part = (size_t)a->batch * a->q_heads * pl.slots * (c->dim + 2) * sizeof(float);
     part = (part + 255) / 256 * 256;
-    return part + (size_t)a->batch * a->kv_heads * sizeof(int32_t);
+    return part + (size_t)a->batch * (pl.qunits ? a->q_heads : a->kv_heads) * sizeof(int32_t);
 }
 
 template <typename K>
@@ -1469,7 +1484,9 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
     if (pl.smem > 227 * 1024) return PKV_ERR_UNSUPPORTED;
     AttnParams p{};
     p.B = a->batch; p.Hq = a->q_heads; p.Hkv = a->kv_heads; p.S = a->seq_len;
-    p.G = a->q_heads / a->kv_heads; p.m = c->dim / 3; p.dim = c->dim;
+    p.G = pl.qunits ? 1 : a->q_heads / a->kv_heads; p.m = c->dim / 3; p.dim = c->dim;
+    p.Hu = pl.qunits ? a->q_heads : a->kv_heads;
+    p.Gq = pl.qunits ? a->q_heads / a->kv_heads : 1;
     p.q = a->q; p.qdt = a->q_dtype; p.q_bs = a->q_batch_stride; p.q_hs = a->q_head_stride;
     p.kc = static_cast<const uint8_t*>(a->k_codes); p.vc = static_cast<const uint8_t*>(a->v_codes);
     p.kv_bs = a->kv_batch_stride; p.kv_hs = a->kv_head_stride;
@@ -1498,7 +1515,7 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
     p.Cz = 1 << c->bits_z;
     p.n_xy = (c->xy_per_z ? p.Cz : 1) << p.bits_flat;
     p.r_max = c->r_max;
-    p.num_items = pl.bal ? (int)std::min<int64_t>(pl.tiles, INT32_MAX) : a->batch * a->kv_heads * pl.nsplit;
+    p.num_items = pl.bal ? (int)std::min<int64_t>(pl.tiles, INT32_MAX) : a->batch * p.Hu * pl.nsplit;
     p.stages = pl.stages;
     if (p.num_items == 0) return PKV_OK;
     if (pl.mha12) return launch_kernel(attn_mha12_kernel, p, pl, st);

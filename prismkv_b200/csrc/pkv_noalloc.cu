@@ -10,7 +10,7 @@
 //
 // Scratch layout (kNoallocBytes, 256-byte aligned, one copy per device):
 //   [0, kCountOff)               split partials, placed so they END at kCountOff
-//   [kCountOff, kNoallocBytes)   one int32 arrival counter per (batch, kv head)
+//   [kCountOff, kNoallocBytes)   one int32 arrival counter per (batch, unit head)
 // The counters are the only part that must be zero when a kernel starts.  The
 // array is zero at module load, the first call on each device zeroes the
 // counter region again, and every kernel leaves each counter it used at zero
@@ -26,6 +26,8 @@
 #include "pkv_common.cuh"
 
 namespace pkv {
+
+size_t attn_counter_bytes(const pkv_codec* c, const pkv_attn_args* a);
 
 constexpr size_t kNoallocBytes = PKV_NOALLOC_SCRATCH_BYTES;
 constexpr size_t kCountOff = kNoallocBytes - (size_t)PKV_NOALLOC_MAX_KV_ROWS * sizeof(int32_t);
@@ -60,7 +62,7 @@ static int noalloc_scratch(cudaStream_t st, unsigned char** out) {
 extern "C" int pkv_attn_decode_noalloc(const pkv_codec* c, const pkv_attn_args* a, void* stream) {
     const size_t need = pkv_attn_workspace_size(c, a);   // 0 for invalid arguments or one split
     if (need == 0) return pkv_attn_decode(c, a, nullptr, 0, stream);
-    const size_t counters = (size_t)a->batch * a->kv_heads * sizeof(int32_t);
+    const size_t counters = pkv::attn_counter_bytes(c, a);
     const size_t part = need - counters;                  // partial bytes, a multiple of 256
     if (part > pkv::kCountOff || counters > pkv::kNoallocBytes - pkv::kCountOff) return PKV_ERR_SCRATCH_LIMIT;
     cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -200,7 +200,7 @@ def test_attention_shapes_in_turn_share_workspace(cuda_ready):
 
 @pytest.mark.parametrize("B,Hq,Hkv,S,variant,bits,kernel", [
     (8, 32, 32, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),
-    (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_polar_kernel"),
+    (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),        # grouped heads, one query head per unit
     (2, 8, 8, 4096, "v1", (3, 3, 2), "attn_polar_kernel"),
     (2, 8, 8, 4096, "lloyd_bias", (4, 4, 4), "attn_polar_kernel"),
     (2, 32, 8, 4096, "learned_bias", (4, 4, 4), "attn_lut_kernel"),
