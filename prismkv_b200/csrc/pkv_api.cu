@@ -15,6 +15,7 @@ int launch_decode(const pkv_codec* c, const void* codes, int cb, int64_t n, int6
                   int64_t os, int64_t group_rows, int64_t group_stride, cudaStream_t st);
 size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a);
 void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out);
+bool attn_group_supported(const pkv_codec* c, const pkv_attn_args* a);
 int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_lse_combine(const pkv_codec* c, const float* parts, int n_parts, int64_t part_stride, int rows,
                        float* out, int64_t out_rs, cudaStream_t st);
@@ -155,7 +156,7 @@ static int check_attn(const pkv_codec* c, const pkv_attn_args* a, bool need_out 
     if (!a) return PKV_ERR_INVALID;
     if (a->batch < 0 || a->q_heads < 0 || a->kv_heads < 0 || a->seq_len < 0) return PKV_ERR_INVALID;
     if (a->kv_heads == 0 || a->q_heads == 0 || a->q_heads % a->kv_heads != 0) return PKV_ERR_INVALID;
-    if (a->q_heads / a->kv_heads > 8) return PKV_ERR_UNSUPPORTED;
+    if (a->q_heads / a->kv_heads > 16) return PKV_ERR_UNSUPPORTED;   // > 8 only where the plan allows (below)
     if (a->code_bytes != 1 && a->code_bytes != 2) return PKV_ERR_INVALID;
     if (!code_bits_fit(c, a->code_bytes)) return PKV_ERR_INVALID;
     if (c->bits_z + c->bits_r + c->bits_theta > 12) return PKV_ERR_UNSUPPORTED;
@@ -171,7 +172,7 @@ static int check_attn(const pkv_codec* c, const pkv_attn_args* a, bool need_out 
 }
 
 size_t pkv_attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a) {
-    if (check_attn(c, a) != PKV_OK || a->batch == 0) return 0;
+    if (check_attn(c, a) != PKV_OK || a->batch == 0 || !pkv::attn_group_supported(c, a)) return 0;
     return pkv::attn_workspace_size(c, a);
 }
 
@@ -179,6 +180,7 @@ int pkv_attn_describe(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan*
     if (!out) return PKV_ERR_INVALID;
     const int rc = check_attn(c, a, false);     // output pointers are not needed to plan
     if (rc) return rc;
+    if (!pkv::attn_group_supported(c, a)) return PKV_ERR_UNSUPPORTED;
     pkv::describe_attn(c, a, out);
     return PKV_OK;
 }

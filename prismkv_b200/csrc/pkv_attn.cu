@@ -1289,6 +1289,12 @@ static int num_sms() {
 
 static int round_group(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 
+}  // namespace pkv
+
+#include "pkv_attn_tc.cu"
+
+namespace pkv {
+
 struct AttnPlan {
     bool mha12;                        // attn_mha12_kernel
     bool polar;                        // attn_polar_kernel, else attn_lut_kernel
@@ -1296,6 +1302,7 @@ struct AttnPlan {
     bool tma;
     bool bal;                          // balanced tile ranges instead of round-robin items
     bool qunits;                       // one unit per query head (grouped heads in the one-head kernel)
+    bool tc;                           // attn_tc_kernel (tensor cores, bf16/fp16 queries)
     int tpu, seg_cap, slots;           // tiles per unit, tiles per segment at most, partial slots
     int64_t tiles, grid;               // balanced: total tiles, CTAs
 };
@@ -1321,7 +1328,24 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     // of the same codes hit L2), which beats per-token work for the whole group at 12-bit codes
     pl.qunits = pl.mha12 && a->q_heads != a->kv_heads;
     if (pl.mha12) pl.G = 1;
-    if (pl.mha12) {
+    {
+        const int n_xy = (c->xy_per_z ? Cz : 1) << (c->bits_r + c->bits_theta);
+        // measured: grouped heads (one decode per KV token serves the whole group) and per-z-bin
+        // tables gain on tensor cores; a single uniform-polar head is faster on the polar kernel
+        pl.tc = !pl.mha12 && pl.tma && c->dim == 96 && (a->q_dtype == PKV_BF16 || a->q_dtype == PKV_F16) &&
+                (a->code_bytes == 1 || a->code_bytes == 2) && n_xy <= 4096 && Cz <= 256 &&
+                a->q_heads / a->kv_heads <= 16 && (a->q_heads > a->kv_heads || c->xy_per_z != 0);
+    }
+    if (pl.tc) {
+        pl.polar = false;
+        pl.TPL = 1;
+        pl.tt = atc::TT;
+        pl.threads = atc::THREADS;
+        pl.stages = atc::STAGES;
+        pl.smem = atc::SMEM_BYTES;
+        pl.chunk = 1 << 30;                // online softmax: no cap on the tokens of an item
+        pl.ctas_per_sm = 1;
+    } else if (pl.mha12) {
         pl.TPL = 1;
         pl.tt = mha12::TT;
         pl.threads = mha12::W * 32 + 32;
@@ -1358,6 +1382,9 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     const int max_tiles_item = std::max(1, pl.chunk / pl.tt);
     const int64_t units = (int64_t)a->batch * (pl.qunits ? a->q_heads : a->kv_heads);
     const int64_t grid = (int64_t)num_sms() * pl.ctas_per_sm;
+    // fixed cost of an item in tile units: the tensor-core kernel's items also rotate the group's
+    // queries through global R and merge their splits, about eight of its 128-token tiles
+    const double item_cost = pl.tc ? 8.0 : 1.0;
     int best = 0;
     double best_cost = 1e300;
     const int min_split = a->num_splits > 0 ? a->num_splits : (tiles_total + max_tiles_item - 1) / max_tiles_item;
@@ -1367,7 +1394,7 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
         if (tiles_per > max_tiles_item) continue;
         const int64_t items = units * ns;
         const int64_t rounds = (items + grid - 1) / grid;
-        const double cost = (double)rounds * (tiles_per + 1.0) + (ns > 1 ? 0.25 : 0.0);
+        const double cost = (double)rounds * (tiles_per + item_cost) + (ns > 1 ? 0.25 : 0.0);
         if (cost < best_cost - 1e-9) { best_cost = cost; best = ns; }
     }
     if (best == 0) best = (tiles_total + max_tiles_item - 1) / max_tiles_item;
@@ -1379,7 +1406,7 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     // CTA's range spans at most ceil(per / cap) + 1 segments, each paying the item overhead
     // Measured on B200: it pays for the one-pass LUT kernel, whose items carry no per-item
     // score pass; the two-pass kernels' per-item fixed cost (~6 us) outweighs the balance.
-    if (!pl.polar && a->seq_lens == nullptr && a->num_splits == 0 && a->seq_len > 0) {
+    if (!pl.polar && !pl.tc && !pl.mha12 && a->seq_lens == nullptr && a->num_splits == 0 && a->seq_len > 0) {
         const int64_t T = units * tiles_total;
         const int64_t G = std::min<int64_t>(grid, T);
         const int64_t per = (T + G - 1) / G;
@@ -1401,9 +1428,16 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     return pl;
 }
 
+// Groups above 8 query heads per KV head run only on the kernels that do not unroll over the group.
+bool attn_group_supported(const pkv_codec* c, const pkv_attn_args* a) {
+    if (a->q_heads / a->kv_heads <= 8) return true;
+    const AttnPlan pl = plan_attn(c, a);
+    return pl.tc || pl.mha12;
+}
+
 void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out) {
     const AttnPlan pl = plan_attn(c, a);
-    out->kernel = pl.mha12 ? PKV_KERNEL_MHA12 : (pl.polar ? PKV_KERNEL_POLAR : PKV_KERNEL_LUT);
+    out->kernel = pl.tc ? PKV_KERNEL_TC : pl.mha12 ? PKV_KERNEL_MHA12 : (pl.polar ? PKV_KERNEL_POLAR : PKV_KERNEL_LUT);
     out->num_splits = pl.nsplit;
     out->tokens_per_split = pl.chunk;
     out->balanced = pl.bal ? 1 : 0;
@@ -1481,6 +1515,7 @@ static int launch_lut(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) 
 
 int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
     AttnPlan pl = plan_attn(c, a);
+    if (a->q_heads / a->kv_heads > 8 && !pl.tc && !pl.mha12) return PKV_ERR_UNSUPPORTED;
     if (pl.smem > 227 * 1024) return PKV_ERR_UNSUPPORTED;
     AttnParams p{};
     p.B = a->batch; p.Hq = a->q_heads; p.Hkv = a->kv_heads; p.S = a->seq_len;
@@ -1518,6 +1553,8 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
     p.num_items = pl.bal ? (int)std::min<int64_t>(pl.tiles, INT32_MAX) : a->batch * p.Hu * pl.nsplit;
     p.stages = pl.stages;
     if (p.num_items == 0) return PKV_OK;
+    if (pl.tc) return a->code_bytes == 1 ? launch_kernel(attn_tc_kernel<1>, p, pl, st)
+                                         : launch_kernel(attn_tc_kernel<2>, p, pl, st);
     if (pl.mha12) return launch_kernel(attn_mha12_kernel, p, pl, st);
     if (pl.polar) return a->code_bytes == 1 ? launch_polar<1>(p, pl, st) : launch_polar<2>(p, pl, st);
     return a->code_bytes == 1 ? launch_lut<1>(p, pl, st) : launch_lut<2>(p, pl, st);

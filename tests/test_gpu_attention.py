@@ -18,6 +18,7 @@ from prismkv_b200.synthetic import synthetic_bias, synthetic_codebook
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 TOL = 1e-3
+TOL_TC = 2e-2       # bf16 / fp16 queries on the tensor-core kernel (bf16 operands): the stated bf16 bound
 
 
 def test_attention_matches_reference_polar_attention(cuda_ready):
@@ -98,7 +99,9 @@ def test_attention_matches_oracle(cuda_ready, B, Hq, Hkv, S, variant, bits, qdt,
     out = decode_attention(q, qv, kc, vc, num_splits=splits)
     ref = oracle.attention(qv.float().cpu().numpy(), kc.cpu().numpy().astype(np.int64),
                            vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
-    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+    plan = q.codec(torch.device(DEV)).describe(qv, kc, vc)
+    tol = TOL_TC if plan["kernel"] == "attn_tc_kernel" else TOL
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=tol, rtol=0)
 
 
 @pytest.mark.parametrize("dim", [66, 192, 129])
