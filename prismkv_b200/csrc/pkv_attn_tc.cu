@@ -104,7 +104,9 @@ template <int CB>
 __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) {
     using namespace atc;
     extern __shared__ uint8_t atc_smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(atc_smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base for the swizzled operands, derived from the array itself (pointer plus
+    // offset) so that every access below stays a shared-memory access
+    uint8_t* smem = atc_smem_raw + ((1024u - (smem_u32(atc_smem_raw) & 1023u)) & 1023u);
     const uint32_t sb = smem_u32(smem);
     float* lutz = reinterpret_cast<float*>(smem + OFF_LUTZ);
     float2* lutxy = reinterpret_cast<float2*>(smem + OFF_LUTXY);
@@ -190,8 +192,8 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
             ItemRange r;
             auto scores = [&](int t) {
                 const int b = t & 1;
-                if (alive && !mbar_wait(&kh_full[b], (t >> 1) & 1, kErrWaitFull)) alive = false;
-                if (alive && t >= 2 && !mbar_wait(&s_empty[b], ((t >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
+                if (alive && !mbar_wait_spin(&kh_full[b], (t >> 1) & 1, kErrWaitFull)) alive = false;
+                if (alive && t >= 2 && !mbar_wait_spin(&s_empty[b], ((t >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
                 if (!alive) return;
                 etc::tc_fence_after();
                 #pragma unroll
@@ -203,9 +205,9 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
             };
             auto pv = [&](int t) {
                 const int b = t & 1;
-                if (alive && !mbar_wait(&p_full[b], (t >> 1) & 1, kErrWaitFull)) alive = false;
-                if (alive && !mbar_wait(&vh_full[b], (t >> 1) & 1, kErrWaitFull)) alive = false;
-                if (alive && t >= 2 && !mbar_wait(&o_empty[b], ((t >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
+                if (alive && !mbar_wait_spin(&p_full[b], (t >> 1) & 1, kErrWaitFull)) alive = false;
+                if (alive && !mbar_wait_spin(&vh_full[b], (t >> 1) & 1, kErrWaitFull)) alive = false;
+                if (alive && t >= 2 && !mbar_wait_spin(&o_empty[b], ((t >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
                 if (!alive) return;
                 etc::tc_fence_after();
                 #pragma unroll
@@ -219,7 +221,7 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
             while (work_next<false>(p, wc, r)) {
                 const int nt = (r.tok1 - r.tok0 + TT - 1) / TT;
                 if (nt == 0) continue;
-                if (alive && !mbar_wait(q_ready, items & 1, kErrWaitFull)) alive = false;
+                if (alive && !mbar_wait_spin(q_ready, items & 1, kErrWaitFull)) alive = false;
                 ++items;
                 scores(it);
                 for (int j = 0; j < nt; ++j) {
@@ -229,7 +231,7 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
                 it += nt;
             }
             // the last MMAs must be complete before tensor memory is freed
-            if (it > 0) mbar_wait(&o_full[(it - 1) & 1], ((it - 1) >> 1) & 1, kErrWaitDrain);
+            if (it > 0) mbar_wait_spin(&o_full[(it - 1) & 1], ((it - 1) >> 1) & 1, kErrWaitDrain);
         }
     } else if (warp >= 2 + SM_WARPS) {
         // ---------------- decoders: codes -> bf16 Khat / Vhat ----------------
@@ -242,9 +244,9 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
             const int nt = (r.tok1 - r.tok0 + TT - 1) / TT;
             for (int j = 0; j < nt; ++j, ++it, ++seq) {
                 const int s = seq % STAGES, b = it & 1;
-                if (alive && !mbar_wait(&full[s], (seq / STAGES) & 1, kErrWaitFull)) alive = false;
-                if (alive && it >= 2 && !mbar_wait(&kh_empty[b], ((it >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
-                if (alive && it >= 2 && !mbar_wait(&vh_empty[b], ((it >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
+                if (alive && !mbar_wait_spin(&full[s], (seq / STAGES) & 1, kErrWaitFull)) alive = false;
+                if (alive && it >= 2 && !mbar_wait_spin(&kh_empty[b], ((it >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
+                if (alive && it >= 2 && !mbar_wait_spin(&vh_empty[b], ((it >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
                 if (alive) {
                     const uint8_t* stage = smem + OFF_STAGE + s * STAGE;
                     #pragma unroll 1
@@ -332,8 +334,8 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
                 // ---- softmax of tile j ----
                 if (j < nt) {
                     const int t = it + j, b = t & 1;
-                    bool ok = alive && mbar_wait(&s_full[b], (t >> 1) & 1, kErrWaitFull);
-                    if (ok && t >= 2) ok = mbar_wait(&p_empty[b], ((t >> 1) - 1) & 1, kErrWaitEmpty);
+                    bool ok = alive && mbar_wait_spin(&s_full[b], (t >> 1) & 1, kErrWaitFull);
+                    if (ok && t >= 2) ok = mbar_wait_spin(&p_empty[b], ((t >> 1) - 1) & 1, kErrWaitEmpty);
                     alive = __all_sync(0xffffffffu, ok) && alive;
                     float sv[NG];
                     if (alive) {
@@ -379,7 +381,7 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
                 // ---- accumulate tile j - 1 ----
                 if (j >= 1) {
                     const int t = it + j - 1, b = t & 1;
-                    bool ok = alive && mbar_wait(&o_full[b], (t >> 1) & 1, kErrWaitFull);
+                    bool ok = alive && mbar_wait_spin(&o_full[b], (t >> 1) & 1, kErrWaitFull);
                     alive = __all_sync(0xffffffffu, ok) && alive;
                     float ov[NG];
                     if (alive) {

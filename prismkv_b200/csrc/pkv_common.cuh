@@ -160,6 +160,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int32_
     return false;
 }
 
+// The same wait without a suspend-time hint: try_wait returns after a short
+// hardware-defined interval, so the phase is seen sooner (tensor-core commits
+// arrive in bursts); the bound is counted in polls (~2^22, a few seconds).
+__device__ __forceinline__ bool mbar_try_wait_spin(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int32_t err,
+                                               uint32_t limit = (1u << 22)) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait_spin(bar, parity)) return true;
+    flag_error(err);
+    return false;
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -113,7 +113,9 @@ template <int CB>
 __global__ void __launch_bounds__(THREADS, 1)
 encode_tc_kernel(CodecArgs a, const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_r) {
     extern __shared__ uint8_t etc_smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(etc_smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base for the swizzled operands, derived from the array itself (pointer plus
+    // offset) so that every access below stays a shared-memory access
+    uint8_t* smem = etc_smem_raw + ((1024u - (smem_u32(etc_smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
     float* thr = reinterpret_cast<float*>(smem + OFF_THR);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ((OFF_BAR + 7) & ~7));
@@ -224,7 +226,11 @@ encode_tc_kernel(CodecArgs a, const __grid_constant__ CUtensorMap tmap_x, const 
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
             const int b = it & 1;
             // warp-uniform: tcgen05.ld below is .sync.aligned, so all lanes go on or none does
-            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[b], (it >> 1) & 1, kErrWaitFull))) break;
+            // spin waits measured faster for the uniform-polar epilogue, the hinted wait for the
+            // (longer) learned-codebook one
+            const bool got = a.xy_mode == 0 ? mbar_wait_spin(&acc_full[b], (it >> 1) & 1, kErrWaitFull)
+                                            : mbar_wait(&acc_full[b], (it >> 1) & 1, kErrWaitFull);
+            if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             float v[3 * TRI];
             const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * 128 + slice * 3 * TRI);
