@@ -226,15 +226,23 @@ def bench_decode(args, ws, rank, device):
     mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
 
+    graphs = []
+    exchange = None
+    if mode == "sequence" and args.exchange == "peer":
+        from prismkv_b200.dist import PeerExchange
+        exchange = PeerExchange(B * Hq, D, device)
+
+    def seq_step():
+        split_sequence_decode(quant, q, kc, vc, out=out, exchange=exchange)
+
     def step(i=None):
         if i is not None:
             starts[i].record(stream)
         if mode == "sequence":
-            # split_sequence_decode, spelled out to time the attention kernel on its own
-            part = codec.attention(q, kc, vc, partial=True)
-            if i is not None:
-                mids[i].record(stream)
-            codec.combine(gather_partials(part.view(B * Hq, D + 2)), out=out.view(B * Hq, D))
+            if graphs:
+                graphs[(i or 0) % len(graphs)].replay()
+            else:
+                seq_step()
         else:
             codec.attention(q, kc, vc, out=out)
         if i is not None:
@@ -243,6 +251,31 @@ def bench_decode(args, ws, rank, device):
     for _ in range(args.warmup):
         scrub()
         step()
+    torch.cuda.synchronize(device)
+    attn_only_ms = None
+    if mode == "sequence":
+        # the attention kernel alone (roofline), then the three launches of a step captured in one
+        # CUDA graph, so the host's launch gaps between them leave the timed step
+        ks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(20)]
+        for a_, b_ in ks:
+            scrub()
+            a_.record(stream)
+            codec.attention(q, kc, vc, partial=True)
+            b_.record(stream)
+        torch.cuda.synchronize(device)
+        attn_only_ms = sum(a_.elapsed_time(b_) for a_, b_ in ks) / len(ks)
+        _barrier(ws)
+        # two graphs: the peer exchange alternates between two buffer halves from call to call
+        for _ in range(2 if exchange is not None else 1):
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_):
+                seq_step()
+            graphs.append(g_)
+        torch.cuda.synchronize(device)
+        _barrier(ws)
+        for j in range(4):
+            scrub()
+            graphs[j % len(graphs)].replay()
     torch.cuda.synchronize(device)
     _barrier(ws)
     torch.cuda.synchronize(device)
@@ -255,10 +288,7 @@ def bench_decode(args, ws, rank, device):
         wall = time.perf_counter() - wall0
     _barrier(ws)
     step_ms = [s_.elapsed_time(e) for s_, e in zip(starts, ends)]
-    if mode == "sequence":                                                  # the attention kernel alone
-        kern_ms = [s_.elapsed_time(m) for s_, m in zip(starts, mids)]
-    else:
-        kern_ms = step_ms
+    kern_ms = [attn_only_ms] if mode == "sequence" else step_ms            # the attention kernel alone
     local_ms = sum(step_ms) / len(step_ms)
     local_kern_ms = sum(kern_ms) / len(kern_ms)
     ms = _max_over_ranks(local_ms, ws, device)
@@ -289,7 +319,7 @@ def bench_decode(args, ws, rank, device):
         d_vc.copy_(h_vc, non_blocking=True)
         d_q.copy_(h_q, non_blocking=True)
         if mode == "sequence":
-            o = split_sequence_decode(quant, d_q, d_kc, d_vc)
+            o = split_sequence_decode(quant, d_q, d_kc, d_vc, exchange=exchange)
         else:
             o = decode_attention(quant, d_q, d_kc, d_vc)
         h_out.copy_(o, non_blocking=True)
@@ -336,6 +366,10 @@ def bench_decode(args, ws, rank, device):
     }
     if mode == "sequence":
         line["attn_ms_per_step"] = round(local_kern_ms, 5)
+        line["config"]["step"] = ("partial attention + " + ("symmetric-memory barrier + peer-read LSE combine"
+                                  if exchange is not None else "NCCL all-gather + LSE combine") +
+                                  ", one CUDA graph per step")
+    graphs.clear()                              # release the graphs holding collectives before teardown
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         gbs, per, tokens, reps = cpu_reference_bandwidth(w, kc, vc, q, quant.R)
         line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
@@ -498,6 +532,8 @@ def main(argv=None):
     ap.add_argument("--mode", default="decode", choices=["decode", "encode"])
     ap.add_argument("--encode-workload", default="learned-gqa", choices=["learned-gqa", "phi3-decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="split-sequence exchange: symmetric-memory peer reads or an NCCL all-gather")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

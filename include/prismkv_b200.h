@@ -224,6 +224,15 @@ PKV_API int pkv_lse_combine(const pkv_codec *c, const float *partials, int32_t n
                     int64_t part_stride, int32_t rows, float *out,
                     int64_t out_row_stride, void *stream);
 
+/* pkv_lse_combine with each part behind its own pointer: `part_ptrs` is a
+ * DEVICE array of n_parts pointers; part p of row r is at
+ * part_ptrs[p] + part_offset + r*(dim+2).  The pointers may name peer GPUs'
+ * buffers mapped over NVLink (split-sequence decode: every rank reads all
+ * ranks' partials directly, after a barrier, instead of an all-gather).   */
+PKV_API int pkv_lse_combine_gather(const pkv_codec *c, const float *const *part_ptrs, int32_t n_parts,
+                           int64_t part_offset, int32_t rows, float *out, int64_t out_row_stride,
+                           void *stream);
+
 /* Scores of prismkv_cuda.polar_attn_fwd: out[b,h,i,j] =
  * scale * <q_rot[b,h,i], dequant(k_codes[b,h,j])> with the uniform polar
  * dequant.  q_params (host): {z_min, delta_z, r_max, delta_r, delta_theta,

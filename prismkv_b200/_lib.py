@@ -24,7 +24,7 @@ DTYPE_CODES = {torch.float32: PKV_F32, torch.bfloat16: PKV_BF16, torch.float16: 
 EXPORTED = ("pkv_abi_version", "pkv_strerror", "pkv_device_error", "pkv_encode", "pkv_decode",
             "pkv_attn_workspace_size", "pkv_workspace_init", "pkv_attn_decode", "pkv_lse_combine",
             "pkv_polar_scores", "pkv_attn_decode_noalloc", "pkv_attn_describe", "pkv_encode_append",
-            "pkv_decode_cache")
+            "pkv_decode_cache", "pkv_lse_combine_gather")
 
 
 class PkvCodec(ctypes.Structure):
@@ -89,6 +89,9 @@ def _declare(lib):
     lib.pkv_attn_describe.argtypes = [P(PkvCodec), P(PkvAttnArgs), P(PkvAttnPlan)]
     lib.pkv_lse_combine.restype = c_int32
     lib.pkv_lse_combine.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int32, c_void_p, c_int64, c_void_p]
+    lib.pkv_lse_combine_gather.restype = c_int32
+    lib.pkv_lse_combine_gather.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int32, c_void_p, c_int64,
+                                           c_void_p]
     lib.pkv_polar_scores.restype = c_int32
     lib.pkv_polar_scores.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
                                      P(c_float), P(c_int32), c_void_p, c_void_p]

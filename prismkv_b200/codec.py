@@ -242,7 +242,8 @@ class DeviceCodec:
     def attention(self, q: torch.Tensor, k_codes: torch.Tensor, v_codes: torch.Tensor,
                   scale: Optional[float] = None, seq_lens: Optional[torch.Tensor] = None,
                   out: Optional[torch.Tensor] = None, num_splits: int = 0,
-                  partial: bool = False, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  partial: bool = False, workspace: Optional[torch.Tensor] = None,
+                  partial_out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Decode attention over packed codes.
 
         q (B, Hq, dim) [or (B, Hq, 1, dim)], k/v codes (B, Hkv, S, m) with unit
@@ -275,11 +276,16 @@ class DeviceCodec:
             scale = self.dim ** -0.5
         if seq_lens is not None:
             seq_lens = seq_lens.to(device=self.device, dtype=torch.int32).contiguous()
-        partial_out = None
         if partial:
-            partial_out = torch.empty((B, Hq, self.dim + 2), dtype=torch.float32, device=self.device)
-        elif out is None:
-            out = torch.empty((B, Hq, self.dim), dtype=torch.float32, device=self.device)
+            if partial_out is None:
+                partial_out = torch.empty((B, Hq, self.dim + 2), dtype=torch.float32, device=self.device)
+            elif (partial_out.dtype != torch.float32 or partial_out.numel() != B * Hq * (self.dim + 2)
+                  or not partial_out.is_contiguous()):
+                raise ValueError("partial_out must be a contiguous float32 tensor of B * Hq * (dim + 2)")
+        else:
+            partial_out = None
+            if out is None:
+                out = torch.empty((B, Hq, self.dim), dtype=torch.float32, device=self.device)
         a = self._attn_args(q, k_codes, v_codes, scale, seq_lens, out, num_splits, partial_out)
         lib = _lib.load()
         with torch.cuda.device(self.device):
@@ -290,6 +296,18 @@ class DeviceCodec:
                                      ws.numel() if ws is not None else 0, self._stream())
         _lib.check(rc, "pkv_attn_decode")
         return partial_out if partial else out
+
+    def combine_gather(self, part_ptrs: int, n_parts: int, part_offset: int, rows: int,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Merge partials that live behind a device array of n_parts pointers (peer buffers)."""
+        if out is None:
+            out = torch.empty((rows, self.dim), dtype=torch.float32, device=self.device)
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            rc = lib.pkv_lse_combine_gather(ctypes.byref(self.struct), part_ptrs, n_parts, part_offset, rows,
+                                            out.data_ptr(), out.stride(0), self._stream())
+        _lib.check(rc, "pkv_lse_combine_gather")
+        return out
 
     def combine(self, partials: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Merge (n_parts, rows, dim + 2) partials into (rows, dim) outputs (with R applied)."""

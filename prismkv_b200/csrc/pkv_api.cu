@@ -19,6 +19,8 @@ bool attn_group_supported(const pkv_codec* c, const pkv_attn_args* a);
 int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_lse_combine(const pkv_codec* c, const float* parts, int n_parts, int64_t part_stride, int rows,
                        float* out, int64_t out_rs, cudaStream_t st);
+int launch_lse_combine_gather(const pkv_codec* c, const float* const* part_ptrs, int n_parts, int64_t part_offset,
+                              int rows, float* out, int64_t out_rs, cudaStream_t st);
 int launch_polar_scores(const float* q, const void* kc, int cb, int B, int H, int Sq, int Sk, int dim,
                         const float* qp, const int32_t* bits, float* out, cudaStream_t st);
 }  // namespace pkv
@@ -210,6 +212,17 @@ int pkv_lse_combine(const pkv_codec* c, const float* partials, int32_t n_parts, 
     if (n_parts > 1 && part_stride < (int64_t)rows * (c->dim + 2)) return PKV_ERR_INVALID;
     return pkv::launch_lse_combine(c, partials, n_parts, part_stride, rows, out, out_row_stride,
                                    static_cast<cudaStream_t>(stream));
+}
+
+int pkv_lse_combine_gather(const pkv_codec* c, const float* const* part_ptrs, int32_t n_parts, int64_t part_offset,
+                           int32_t rows, float* out, int64_t out_row_stride, void* stream) {
+    if (!c || c->dim <= 0 || c->dim % 3 != 0 || !c->R) return PKV_ERR_INVALID;
+    if (c->dim > 192) return PKV_ERR_UNSUPPORTED;
+    if (n_parts < 1 || rows < 0 || part_offset < 0) return PKV_ERR_INVALID;
+    if (rows == 0) return PKV_OK;
+    if (!part_ptrs || !out || out_row_stride < c->dim) return PKV_ERR_INVALID;
+    return pkv::launch_lse_combine_gather(c, part_ptrs, n_parts, part_offset, rows, out, out_row_stride,
+                                          static_cast<cudaStream_t>(stream));
 }
 
 int pkv_polar_scores(const float* q_rot, const void* k_codes, int32_t code_bytes, int32_t B, int32_t H, int32_t Sq,

@@ -1272,6 +1272,39 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(const float* __restric
     }
 }
 
+// The same merge with each part behind its own pointer: part p of row r at
+// part_ptrs[p] + part_offset + r * (dim + 2).  The pointers may name other GPUs'
+// memory (peer buffers mapped over NVLink); the loads are plain coherent loads
+// that bypass L1 (the buffers are rewritten between calls).
+__global__ void __launch_bounds__(128) lse_combine_gather_kernel(const float* const* __restrict__ part_ptrs,
+                                                                 int n_parts, int64_t part_offset, int rows,
+                                                                 int dim, const float* __restrict__ R,
+                                                                 float* __restrict__ out, int64_t out_rs) {
+    extern __shared__ float fin_g[];               // [dim]
+    const int row = blockIdx.x;
+    if (row >= rows) return;
+    for (int k = threadIdx.x; k < dim; k += blockDim.x) {
+        float M = -INFINITY;
+        for (int pi = 0; pi < n_parts; ++pi)
+            M = fmaxf(M, __ldcg(part_ptrs[pi] + part_offset + (int64_t)row * (dim + 2)));
+        float l = 0.f, v = 0.f;
+        for (int pi = 0; pi < n_parts; ++pi) {
+            const float* src = part_ptrs[pi] + part_offset + (int64_t)row * (dim + 2);
+            const float mp = __ldcg(src);
+            const float f = (mp == -INFINITY) ? 0.f : expf(mp - M);
+            l = fmaf(__ldcg(src + 1), f, l);
+            v = fmaf(__ldcg(src + 2 + k), f, v);
+        }
+        fin_g[k] = (l > 0.f) ? v / l : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        float v = 0.f;
+        for (int k = 0; k < dim; ++k) v = fmaf(fin_g[k], __ldg(R + k * dim + i), v);
+        out[(int64_t)row * out_rs + i] = v;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -1565,6 +1598,14 @@ int launch_lse_combine(const pkv_codec* c, const float* parts, int n_parts, int6
     if (rows == 0) return PKV_OK;
     lse_combine_kernel<<<rows, 128, c->dim * sizeof(float), st>>>(parts, n_parts, part_stride, rows, c->dim,
                                                                    c->R, out, out_rs);
+    return cudaGetLastError() == cudaSuccess ? PKV_OK : PKV_ERR_CUDA;
+}
+
+int launch_lse_combine_gather(const pkv_codec* c, const float* const* part_ptrs, int n_parts, int64_t part_offset,
+                              int rows, float* out, int64_t out_rs, cudaStream_t st) {
+    if (rows == 0) return PKV_OK;
+    lse_combine_gather_kernel<<<rows, 128, c->dim * sizeof(float), st>>>(part_ptrs, n_parts, part_offset, rows,
+                                                                          c->dim, c->R, out, out_rs);
     return cudaGetLastError() == cudaSuccess ? PKV_OK : PKV_ERR_CUDA;
 }
 

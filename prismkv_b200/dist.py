@@ -6,9 +6,11 @@ Two partitionings of the decode-attention path:
   tokens ``shard_range(S, N, r)`` of every (batch, kv head).  Each rank runs
   the fused kernel in partial mode, giving rotated-space softmax partials
   ``[m, l, o]`` (natural-log max, weight sum, unnormalised output) per
-  (batch, q head).  One all-gather exchanges them (NCCL over NVLink; 4 B x
-  (dim + 2) per row and rank), and every rank merges them with
-  ``pkv_lse_combine``, which also applies ``R`` once.  The merge is the
+  (batch, q head).  Either one NCCL all-gather exchanges them (4 B x
+  (dim + 2) per row and rank) and ``pkv_lse_combine`` merges them, or
+  (``PeerExchange``) each rank writes them into symmetric memory and, after
+  one device-side barrier, ``pkv_lse_combine_gather`` reads every rank's rows
+  over NVLink; both apply ``R`` once.  The merge is the
   log-sum-exp rule ``o = sum_i e^(m_i - M) o_i / sum_i e^(m_i - M) l_i``.
 * **Batch shards.**  Rank r holds batch rows ``shard_range(B, N, r)``; the
   ranks share nothing and no collective runs.
@@ -53,19 +55,62 @@ def gather_partials(partials: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+class PeerExchange:
+    """Split-sequence exchange through symmetric memory instead of an all-gather.
+
+    Every rank holds a buffer of `rows` partial rows ([m, l, o_rot], dim + 2
+    floats each) in symmetric memory, twice (calls alternate between the two
+    halves).  The attention kernel writes its partials straight into this
+    rank's half; one device-side barrier makes every rank's partials visible;
+    then every rank's ``pkv_lse_combine_gather`` reads all ranks' rows over
+    NVLink through the peer pointers and merges them.  Alternating halves make
+    one barrier per call enough: a rank rewrites a half only after a later
+    barrier, which every peer reaches after its reads of that half.
+    """
+
+    def __init__(self, rows: int, dim: int, device, group=None):
+        import torch.distributed._symmetric_memory as symm
+        self.group = group or dist.group.WORLD
+        self.rows, self.dim = rows, dim
+        self.slot = rows * (dim + 2)
+        if hasattr(symm, "enable_symm_mem_for_group") and not symm.is_symm_mem_enabled_for_group(
+                self.group.group_name):
+            symm.enable_symm_mem_for_group(self.group.group_name)
+        self.buf = symm.empty(2 * self.slot, dtype=torch.float32, device=device)
+        self.handle = symm.rendezvous(self.buf, self.group.group_name)
+        self.world = self.handle.world_size
+        self.parity = 0
+
+    def next_half(self):
+        """(this rank's half as a (rows, dim + 2) view, its offset in floats) for the next call."""
+        off = self.parity * self.slot
+        self.parity ^= 1
+        return self.buf[off:off + self.slot].view(self.rows, self.dim + 2), off
+
+
 def split_sequence_decode(quantizer, q: torch.Tensor, k_codes: torch.Tensor, v_codes: torch.Tensor,
                           scale: Optional[float] = None, group=None,
-                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                          out: Optional[torch.Tensor] = None,
+                          exchange: Optional[PeerExchange] = None) -> torch.Tensor:
     """Decode attention with the sequence sharded over the ranks of `group`.
 
     q: (B, Hq, dim), identical on every rank.  k_codes / v_codes: this rank's
     (B, Hkv, S_r, m) token shard (S_r may be 0).  Returns (B, Hq, dim) fp32,
     the attention over the concatenation of all ranks' shards in rank order.
+    With `exchange` (a PeerExchange of B * Hq rows) the partials cross NVLink
+    through symmetric memory; otherwise one NCCL all-gather moves them.
     """
     if q.dim() == 4:
         q = q[:, :, 0, :]
     codec = quantizer.codec(q.device)
     B, Hq, D = q.shape
+    if exchange is not None:
+        half, off = exchange.next_half()
+        codec.attention(q, k_codes, v_codes, scale=scale, partial=True, partial_out=half)
+        exchange.handle.barrier(channel=0)
+        res = codec.combine_gather(exchange.handle.buffer_ptrs_dev, exchange.world, off, B * Hq,
+                                   out=None if out is None else out.view(B * Hq, D))
+        return res.view(B, Hq, D)
     part = codec.attention(q, k_codes, v_codes, scale=scale, partial=True)
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         parts = gather_partials(part.view(B * Hq, D + 2), group)
@@ -81,4 +126,4 @@ def batch_shard_decode(quantizer, q: torch.Tensor, k_codes: torch.Tensor, v_code
     return quantizer.codec(q.device).attention(q, k_codes, v_codes, scale=scale, out=out)
 
 
-__all__ = ["shard_range", "gather_partials", "split_sequence_decode", "batch_shard_decode"]
+__all__ = ["shard_range", "gather_partials", "split_sequence_decode", "batch_shard_decode", "PeerExchange"]

@@ -1,4 +1,5 @@
-"""Split-sequence and batch-sharded decode on 2 GPUs (NCCL), against the oracle.
+"""Split-sequence (NCCL all-gather, and symmetric-memory peer reads) and batch-sharded
+decode on 2 GPUs, against the oracle.
 
 Runs only where at least two GPUs are visible; the exchange logic itself is
 also covered on CPU with gloo (test_dist_cpu.py).  NVLS is off in these child
@@ -41,6 +42,11 @@ def _worker(rank, world, port, results):
         ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64),
                                vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
         err_seq = float(np.abs(out.cpu().numpy() - ref).max())
+        from prismkv_b200.dist import PeerExchange
+        ex = PeerExchange(B * Hq, 96, dev)
+        for _ in range(3):                       # both buffer halves, then the first again
+            outp = split_sequence_decode(q, qv, kc[:, :, a:b].contiguous(), vc[:, :, a:b].contiguous(), exchange=ex)
+            err_seq = max(err_seq, float(np.abs(outp.cpu().numpy() - ref).max()))
         ba, bb = shard_range(B, world, rank)
         outb = batch_shard_decode(q, qv[ba:bb].contiguous(), kc[ba:bb].contiguous(), vc[ba:bb].contiguous())
         err_batch = float(np.abs(outb.cpu().numpy() - ref[ba:bb]).max())
