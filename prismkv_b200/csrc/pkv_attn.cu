@@ -1373,7 +1373,11 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
         pl.polar = false;
         pl.TPL = 1;
         pl.tt = atc::TT;
-        pl.threads = atc::THREADS;
+        {
+            const int g = a->q_heads / a->kv_heads;
+            pl.G = g <= 4 ? 4 : (g <= 8 ? 8 : 16);          // register state per head of the group
+        }
+        pl.threads = atc::threads_for(pl.G);
         pl.stages = atc::STAGES;
         pl.smem = atc::SMEM_BYTES;
         pl.chunk = 1 << 30;                // online softmax: no cap on the tokens of an item
@@ -1586,8 +1590,15 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
     p.num_items = pl.bal ? (int)std::min<int64_t>(pl.tiles, INT32_MAX) : a->batch * p.Hu * pl.nsplit;
     p.stages = pl.stages;
     if (p.num_items == 0) return PKV_OK;
-    if (pl.tc) return a->code_bytes == 1 ? launch_kernel(attn_tc_kernel<1>, p, pl, st)
-                                         : launch_kernel(attn_tc_kernel<2>, p, pl, st);
+    if (pl.tc) {
+        if (a->code_bytes == 1)
+            return pl.G == 4 ? launch_kernel(attn_tc_kernel<1, 4>, p, pl, st)
+                             : pl.G == 8 ? launch_kernel(attn_tc_kernel<1, 8>, p, pl, st)
+                                         : launch_kernel(attn_tc_kernel<1, 16>, p, pl, st);
+        return pl.G == 4 ? launch_kernel(attn_tc_kernel<2, 4>, p, pl, st)
+                         : pl.G == 8 ? launch_kernel(attn_tc_kernel<2, 8>, p, pl, st)
+                                     : launch_kernel(attn_tc_kernel<2, 16>, p, pl, st);
+    }
     if (pl.mha12) return launch_kernel(attn_mha12_kernel, p, pl, st);
     if (pl.polar) return a->code_bytes == 1 ? launch_polar<1>(p, pl, st) : launch_polar<2>(p, pl, st);
     return a->code_bytes == 1 ? launch_lut<1>(p, pl, st) : launch_lut<2>(p, pl, st);

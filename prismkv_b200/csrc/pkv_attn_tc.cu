@@ -29,9 +29,10 @@ constexpr int TT = 128;                    // tokens per tile (MMA M of the scor
 constexpr int D = 96;
 constexpr int NG = 16;                     // MMA N: query heads of the group, padded
 constexpr int STAGES = 3;                  // code ring (K and V of a tile per stage)
-constexpr int DEC_WARPS = 8;
 constexpr int SM_WARPS = 4;                // softmax / accumulate group
-constexpr int THREADS = (2 + SM_WARPS + DEC_WARPS) * 32;
+// decoder warps: 16 when the softmax group's per-head state is small (groups <= 8), else 8
+__host__ __device__ constexpr int dec_warps(int gm) { return gm <= 8 ? 16 : 8; }
+__host__ __device__ constexpr int threads_for(int gm) { return (2 + SM_WARPS + dec_warps(gm)) * 32; }
 constexpr int STAGE = 2 * TT * 64;         // 16 KB: K and V codes, 12-bit in uint16
 constexpr int HCHUNK = TT * 64;            // 8 KB: one 32-column chunk of a decoded tile
 constexpr int KH = 3 * HCHUNK;             // Khat tile
@@ -98,11 +99,30 @@ __device__ __forceinline__ uint16_t half1(float a, bool f16) {
     return (uint16_t)(pack2(a, 0.f, f16) & 0xFFFFu);
 }
 
+// N consecutive fp32 columns (N = 4, 8, 16) of this thread's TMEM lane
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v) {
+    if constexpr (N == 16) {
+        etc::tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(v));
+    } else if constexpr (N == 8) {
+        etc::tmem_ld8(taddr, v);
+    } else {
+        uint32_t r[4];
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(taddr));
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+    }
+}
+
 }  // namespace atc
 
-template <int CB>
-__global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) {
+// GM: register state per query head of the group (4, 8 or 16 >= the group size)
+template <int CB, int GM>
+__global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnParams p) {
     using namespace atc;
+    constexpr int DEC_WARPS = dec_warps(GM);
+    constexpr int THREADS = threads_for(GM);
     extern __shared__ uint8_t atc_smem_raw[];
     // 1024-byte aligned base for the swizzled operands, derived from the array itself (pointer plus
     // offset) so that every access below stays a shared-memory access
@@ -249,22 +269,26 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
                 if (alive && it >= 2 && !mbar_wait_spin(&vh_empty[b], ((it >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
                 if (alive) {
                     const uint8_t* stage = smem + OFF_STAGE + s * STAGE;
+                    // thread -> (token t0 + i * TSTEP, triplet pair jp); the swizzle key (t >> 1) & 3 is the
+                    // same for all its tokens (TSTEP is a multiple of 8), so the three store offsets are
+                    // fixed and advance by TSTEP rows per step
+                    constexpr int NTH = DEC_WARPS * 32, TSTEP = NTH / 16;
+                    const int jp = dt & 15, t0 = dt >> 4;
+                    const uint32_t o0 = sw_off(t0, 6 * jp, HCHUNK), o1 = sw_off(t0, 6 * jp + 2, HCHUNK),
+                                   o2 = sw_off(t0, 6 * jp + 4, HCHUNK);
                     #pragma unroll 1
                     for (int kv = 0; kv < 2; ++kv) {
-                        const uint8_t* codes = stage + kv * TT * 32 * CB;
+                        const uint8_t* codes = stage + kv * TT * 32 * CB + t0 * 32 * CB + jp * 2 * CB;
                         uint8_t* dst = smem + (kv == 0 ? OFF_KH + b * KH : OFF_VH + b * VH);
-                        const int chunk_bytes = HCHUNK;
-                        // 16 pairs of triplets per token; a warp covers two tokens per step
-                        #pragma unroll 4
-                        for (int w = dt; w < TT * 16; w += DEC_WARPS * 32) {
-                            const int t = w >> 4, jp = w & 15;
+                        #pragma unroll
+                        for (int i = 0; i < TT / TSTEP; ++i) {
                             uint32_t c0, c1;
                             if (CB == 2) {
-                                const uint32_t word = *reinterpret_cast<const uint32_t*>(codes + t * 64 + jp * 4);
+                                const uint32_t word = *reinterpret_cast<const uint32_t*>(codes + i * TSTEP * 64);
                                 c0 = word & 0xFFFFu;
                                 c1 = word >> 16;
                             } else {
-                                const uint32_t half = *reinterpret_cast<const uint16_t*>(codes + t * 32 + jp * 2);
+                                const uint32_t half = *reinterpret_cast<const uint16_t*>(codes + i * TSTEP * 32);
                                 c0 = half & 0xFFu;
                                 c1 = half >> 8;
                             }
@@ -273,10 +297,10 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
                             const float z0 = lutz[c0 >> bf], z1 = lutz[c1 >> bf];
                             const float2 xy0 = lutxy[p.xy_per_z ? c0 : (c0 & fmask)];
                             const float2 xy1 = lutxy[p.xy_per_z ? c1 : (c1 & fmask)];
-                            const int col = 6 * jp;
-                            *reinterpret_cast<uint32_t*>(dst + sw_off(t, col, chunk_bytes)) = pack2(z0, xy0.x, f16);
-                            *reinterpret_cast<uint32_t*>(dst + sw_off(t, col + 2, chunk_bytes)) = pack2(xy0.y, z1, f16);
-                            *reinterpret_cast<uint32_t*>(dst + sw_off(t, col + 4, chunk_bytes)) = pack2(xy1.x, xy1.y, f16);
+                            uint8_t* d = dst + i * TSTEP * 64;
+                            *reinterpret_cast<uint32_t*>(d + o0) = pack2(z0, xy0.x, f16);
+                            *reinterpret_cast<uint32_t*>(d + o1) = pack2(xy0.y, z1, f16);
+                            *reinterpret_cast<uint32_t*>(d + o2) = pack2(xy1.x, xy1.y, f16);
                         }
                     }
                     fence_proxy_async_smem();                 // generic stores -> tensor-core reads
@@ -303,9 +327,9 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
         while (work_next<false>(p, wc, r)) {
             const int ntok = r.tok1 - r.tok0;
             const int nt = (ntok + TT - 1) / TT;
-            float m_run[NG], l_run[NG], acc[NG];
+            float m_run[GM], l_run[GM], acc[GM];
             #pragma unroll
-            for (int g = 0; g < NG; ++g) { m_run[g] = -INFINITY; l_run[g] = 0.f; acc[g] = 0.f; }
+            for (int g = 0; g < GM; ++g) { m_run[g] = -INFINITY; l_run[g] = 0.f; acc[g] = 0.f; }
             if (nt > 0) {
                 // q' = scale log2(e) R q for the group's heads -> bf16 operand rows (rows >= G stay zero)
                 for (int idx = gt; idx < G * D; idx += nthr) {
@@ -337,22 +361,22 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
                     bool ok = alive && mbar_wait_spin(&s_full[b], (t >> 1) & 1, kErrWaitFull);
                     if (ok && t >= 2) ok = mbar_wait_spin(&p_empty[b], ((t >> 1) - 1) & 1, kErrWaitEmpty);
                     alive = __all_sync(0xffffffffu, ok) && alive;
-                    float sv[NG];
+                    float sv[GM];
                     if (alive) {
                         etc::tc_fence_after();
-                        etc::tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * NG), sv);
+                        tmem_ld<GM>(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * NG), sv);
                         etc::tmem_wait_ld();
                         etc::tc_fence_before();
                     } else {
                         #pragma unroll
-                        for (int g = 0; g < NG; ++g) sv[g] = 0.f;
+                        for (int g = 0; g < GM; ++g) sv[g] = 0.f;
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&s_empty[b]);
                     const bool valid = (j * TT + row) < ntok;
                     // tile max per head over the 128 tokens
                     #pragma unroll
-                    for (int g = 0; g < NG; ++g) {
+                    for (int g = 0; g < GM; ++g) {
                         float v = (valid && g < G) ? sv[g] : -INFINITY;
                         #pragma unroll
                         for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
@@ -361,7 +385,7 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
                     named_bar_sync(1, nthr);
                     uint8_t* P = smem + OFF_P + b * PT;
                     #pragma unroll
-                    for (int g = 0; g < NG; ++g) {
+                    for (int g = 0; g < GM; ++g) {
                         if (g >= G) break;
                         float tm = sRed[g];
                         #pragma unroll
@@ -383,27 +407,27 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
                     const int t = it + j - 1, b = t & 1;
                     bool ok = alive && mbar_wait_spin(&o_full[b], (t >> 1) & 1, kErrWaitFull);
                     alive = __all_sync(0xffffffffu, ok) && alive;
-                    float ov[NG];
+                    float ov[GM];
                     if (alive) {
                         etc::tc_fence_after();
-                        etc::tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(32 + b * NG), ov);
+                        tmem_ld<GM>(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(32 + b * NG), ov);
                         etc::tmem_wait_ld();
                         etc::tc_fence_before();
                     } else {
                         #pragma unroll
-                        for (int g = 0; g < NG; ++g) ov[g] = 0.f;
+                        for (int g = 0; g < GM; ++g) ov[g] = 0.f;
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&o_empty[b]);
                     #pragma unroll
-                    for (int g = 0; g < NG; ++g) acc[g] = fmaf(acc[g], sAlpha[b * NG + g], ov[g]);
+                    for (int g = 0; g < GM; ++g) acc[g] = fmaf(acc[g], sAlpha[b * NG + g], ov[g]);
                     // sAlpha[b] is rewritten by the softmax of tile t + 2, which follows this read
                 }
             }
             it += nt;
             // ---- finish: M (log2 units), l, unnormalised rotated output per head ----
             #pragma unroll
-            for (int g = 0; g < NG; ++g) {
+            for (int g = 0; g < GM; ++g) {
                 float l = l_run[g];
                 #pragma unroll
                 for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
@@ -411,15 +435,18 @@ __global__ void __launch_bounds__(atc::THREADS, 1) attn_tc_kernel(AttnParams p) 
             }
             if (row < D) {
                 #pragma unroll
-                for (int g = 0; g < NG; ++g)
+                for (int g = 0; g < GM; ++g)
                     if (g < G) sO[g * D + row] = acc[g];
             }
             named_bar_sync(1, nthr);
-            if (gt < G) {
-                float l = 0.f;
-                for (int q = 0; q < SM_WARPS; ++q) l += sRed[q * NG + gt];
-                sL[gt] = l;
-                sM[gt] = m_run[gt];
+            #pragma unroll
+            for (int g = 0; g < GM; ++g) {
+                if (gt == g && g < G) {
+                    float l = 0.f;
+                    for (int q = 0; q < SM_WARPS; ++q) l += sRed[q * NG + g];
+                    sL[g] = l;
+                    sM[g] = m_run[g];
+                }
             }
             named_bar_sync(1, nthr);
             finish_item(p, r, sM, sL, sO, sFin, sflag, p.R, D, gt, nthr, 1);
