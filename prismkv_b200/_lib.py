@@ -53,7 +53,8 @@ class PkvAttnPlan(ctypes.Structure):
                 ("threads", c_int32), ("smem_bytes", c_int32), ("ctas_per_sm", c_int32), ("balanced", c_int32)]
 
 
-KERNEL_NAMES = {1: "attn_mha12_kernel", 2: "attn_polar_kernel", 3: "attn_lut_kernel", 4: "attn_tc_kernel"}
+KERNEL_NAMES = {1: "attn_mha12_kernel", 2: "attn_polar_kernel", 3: "attn_lut_kernel", 4: "attn_tc_kernel",
+                5: "attn_mha8_kernel"}
 
 _lock = threading.Lock()
 _lib = None

@@ -16,7 +16,6 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libprismkv_b200.so")
-SOURCES = ["pkv_lib.cu", "pkv_codec.cu", "pkv_attn.cu", "pkv_scores.cu", "pkv_api.cu", "pkv_common.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -38,7 +37,9 @@ def _stale() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    deps = [os.path.join(HERE, "csrc", s) for s in SOURCES] + [os.path.join(ROOT, "include", "prismkv_b200.h")]
+    csrc = os.path.join(HERE, "csrc")
+    deps = [os.path.join(csrc, s) for s in os.listdir(csrc) if s.endswith((".cu", ".cuh"))]
+    deps.append(os.path.join(ROOT, "include", "prismkv_b200.h"))
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 

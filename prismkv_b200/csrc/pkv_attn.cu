@@ -1325,11 +1325,13 @@ static int round_group(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
 }  // namespace pkv
 
 #include "pkv_attn_tc.cu"
+#include "pkv_attn_mha8.cu"
 
 namespace pkv {
 
 struct AttnPlan {
     bool mha12;                        // attn_mha12_kernel
+    bool mha8;                         // attn_mha8_kernel
     bool polar;                        // attn_polar_kernel, else attn_lut_kernel
     int G, TPL, stages, nsplit, chunk, tt, threads, smem, ctas_per_sm;
     bool tma;
@@ -1369,6 +1371,14 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
                 (a->code_bytes == 1 || a->code_bytes == 2) && n_xy <= 4096 && Cz <= 256 &&
                 a->q_heads / a->kv_heads <= 16 && (a->q_heads > a->kv_heads || c->xy_per_z != 0);
     }
+    // one-byte uniform-polar codes: one query head per unit, unless tensor cores serve the group
+    pl.mha8 = pl.polar && !pl.tc && c->dim == 96 && a->code_bytes == 1 && c->xy_per_z == 0 &&
+              (c->flags & PKV_CODEC_Z_UNIFORM) != 0 && c->bits_z >= 1 && c->bits_r + c->bits_theta <= 5 &&
+              c->bits_z + c->bits_r + c->bits_theta <= 8;
+    if (pl.mha8) {
+        pl.qunits = a->q_heads != a->kv_heads;
+        pl.G = 1;
+    }
     if (pl.tc) {
         pl.polar = false;
         pl.TPL = 1;
@@ -1382,6 +1392,15 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
         pl.smem = atc::SMEM_BYTES;
         pl.chunk = 1 << 30;                // online softmax: no cap on the tokens of an item
         pl.ctas_per_sm = 1;
+    } else if (pl.mha8) {
+        pl.polar = false;
+        pl.TPL = 1;
+        pl.tt = mha8::TT;
+        pl.threads = mha8::W * 32 + 32;
+        pl.stages = mha8::STAGES;
+        pl.smem = mha8::TOTAL;
+        pl.chunk = 1 << 30;                // online softmax: no cap on the tokens of an item
+        pl.ctas_per_sm = 2;
     } else if (pl.mha12) {
         pl.TPL = 1;
         pl.tt = mha12::TT;
@@ -1421,7 +1440,8 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     const int64_t grid = (int64_t)num_sms() * pl.ctas_per_sm;
     // fixed cost of an item in tile units: the tensor-core kernel's items also rotate the group's
     // queries through global R and merge their splits, about eight of its 128-token tiles
-    const double item_cost = pl.tc ? 8.0 : 1.0;
+    // (query rotation, score table, warp merge and R reload: about three of the one-byte kernel's)
+    const double item_cost = pl.tc ? 8.0 : pl.mha8 ? 3.0 : 1.0;
     int best = 0;
     double best_cost = 1e300;
     const int min_split = a->num_splits > 0 ? a->num_splits : (tiles_total + max_tiles_item - 1) / max_tiles_item;
@@ -1443,7 +1463,7 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     // CTA's range spans at most ceil(per / cap) + 1 segments, each paying the item overhead
     // Measured on B200: it pays for the one-pass LUT kernel, whose items carry no per-item
     // score pass; the two-pass kernels' per-item fixed cost (~6 us) outweighs the balance.
-    if (!pl.polar && !pl.tc && !pl.mha12 && a->seq_lens == nullptr && a->num_splits == 0 && a->seq_len > 0) {
+    if (!pl.polar && !pl.tc && !pl.mha12 && !pl.mha8 && a->seq_lens == nullptr && a->num_splits == 0 && a->seq_len > 0) {
         const int64_t T = units * tiles_total;
         const int64_t G = std::min<int64_t>(grid, T);
         const int64_t per = (T + G - 1) / G;
@@ -1469,12 +1489,15 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
 bool attn_group_supported(const pkv_codec* c, const pkv_attn_args* a) {
     if (a->q_heads / a->kv_heads <= 8) return true;
     const AttnPlan pl = plan_attn(c, a);
-    return pl.tc || pl.mha12;
+    return pl.tc || pl.mha12 || pl.mha8;
 }
 
 void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out) {
     const AttnPlan pl = plan_attn(c, a);
-    out->kernel = pl.tc ? PKV_KERNEL_TC : pl.mha12 ? PKV_KERNEL_MHA12 : (pl.polar ? PKV_KERNEL_POLAR : PKV_KERNEL_LUT);
+    out->kernel = pl.tc      ? PKV_KERNEL_TC
+                  : pl.mha12 ? PKV_KERNEL_MHA12
+                  : pl.mha8  ? PKV_KERNEL_MHA8
+                             : (pl.polar ? PKV_KERNEL_POLAR : PKV_KERNEL_LUT);
     out->num_splits = pl.nsplit;
     out->tokens_per_split = pl.chunk;
     out->balanced = pl.bal ? 1 : 0;
@@ -1552,7 +1575,7 @@ static int launch_lut(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) 
 
 int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
     AttnPlan pl = plan_attn(c, a);
-    if (a->q_heads / a->kv_heads > 8 && !pl.tc && !pl.mha12) return PKV_ERR_UNSUPPORTED;
+    if (a->q_heads / a->kv_heads > 8 && !pl.tc && !pl.mha12 && !pl.mha8) return PKV_ERR_UNSUPPORTED;
     if (pl.smem > 227 * 1024) return PKV_ERR_UNSUPPORTED;
     AttnParams p{};
     p.B = a->batch; p.Hq = a->q_heads; p.Hkv = a->kv_heads; p.S = a->seq_len;
@@ -1600,6 +1623,7 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
                                      : launch_kernel(attn_tc_kernel<2, 16>, p, pl, st);
     }
     if (pl.mha12) return launch_kernel(attn_mha12_kernel, p, pl, st);
+    if (pl.mha8) return launch_kernel(attn_mha8_kernel, p, pl, st);
     if (pl.polar) return a->code_bytes == 1 ? launch_polar<1>(p, pl, st) : launch_polar<2>(p, pl, st);
     return a->code_bytes == 1 ? launch_lut<1>(p, pl, st) : launch_lut<2>(p, pl, st);
 }

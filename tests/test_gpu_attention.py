@@ -79,7 +79,17 @@ CASES = [
     (2, 32, 8, 1000, "learned_bias", (4, 4, 4), torch.bfloat16, 0),  # learned-gqa shape, short
     (1, 4, 4, 700, "lloyd", (4, 4, 4), torch.float32, 0),
     (1, 8, 4, 900, "lloyd_learned_bias", (4, 4, 4), torch.float32, 0),
-    (2, 4, 4, 513, "v1", (3, 3, 2), torch.float32, 0),            # uint8 codes
+    (2, 4, 4, 513, "v1", (3, 3, 2), torch.float32, 0),            # uint8 codes (one-byte kernel)
+    (2, 8, 8, 1, "v1", (3, 3, 2), torch.float32, 0),
+    (2, 8, 8, 255, "v1", (3, 3, 2), torch.bfloat16, 0),
+    (1, 8, 8, 4100, "v1", (3, 3, 2), torch.float32, 3),
+    (2, 16, 4, 777, "v1", (3, 3, 2), torch.float32, 0),           # grouped fp32: one query head per unit
+    (1, 32, 2, 600, "v1", (3, 3, 2), torch.float32, 2),           # group 16
+    (1, 6, 2, 300, "v1", (3, 3, 2), torch.float16, 0),            # grouped fp16: tensor cores
+    (2, 4, 4, 600, "v1", (4, 2, 2), torch.float32, 0),
+    (2, 4, 4, 600, "v1", (3, 2, 3), torch.float32, 0),
+    (2, 4, 4, 600, "v1", (2, 3, 3), torch.float32, 0),            # 64 (r, theta) cells: polar kernel
+    (1, 4, 4, 700, "lloyd", (3, 3, 2), torch.float32, 0),
     (2, 4, 4, 513, "learned", (3, 3, 2), torch.float32, 0),
     (1, 4, 2, 300, "v1", (4, 4, 4), torch.float32, 0),            # group 2
     (1, 16, 2, 300, "v1", (4, 4, 4), torch.float32, 0),           # group 8
@@ -116,8 +126,9 @@ def test_attention_other_head_dims(cuda_ready, dim):
     np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
 
 
-def test_attention_ragged_and_empty_rows(cuda_ready):
-    q, p = _setup("v1", (4, 4, 4))
+@pytest.mark.parametrize("bits", [(4, 4, 4), (3, 3, 2)])
+def test_attention_ragged_and_empty_rows(cuda_ready, bits):
+    q, p = _setup("v1", bits)
     kc, vc = _codes(q, 3, 8, 512, seed=2)
     qv = torch.randn(3, 8, 96, generator=torch.Generator(device=DEV).manual_seed(2), device=DEV)
     lens = torch.tensor([512, 0, 77], dtype=torch.int32, device=DEV)
@@ -204,7 +215,10 @@ def test_attention_shapes_in_turn_share_workspace(cuda_ready):
 @pytest.mark.parametrize("B,Hq,Hkv,S,variant,bits,kernel", [
     (8, 32, 32, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),
     (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),        # grouped heads, one query head per unit
-    (2, 8, 8, 4096, "v1", (3, 3, 2), "attn_polar_kernel"),
+    (2, 8, 8, 4096, "v1", (3, 3, 2), "attn_mha8_kernel"),
+    (2, 32, 8, 4096, "v1", (3, 3, 2), "attn_mha8_kernel"),        # fp32 queries of a group
+    (2, 8, 8, 4096, "v1", (2, 3, 3), "attn_polar_kernel"),
+    (2, 8, 8, 4096, "lloyd", (3, 3, 2), "attn_polar_kernel"),
     (2, 8, 8, 4096, "lloyd_bias", (4, 4, 4), "attn_polar_kernel"),
     (2, 32, 8, 4096, "learned_bias", (4, 4, 4), "attn_lut_kernel"),
 ])
@@ -248,3 +262,20 @@ def test_phi3_decode_full_size(cuda_ready):
     ref = oracle.attention(qv.float().cpu().numpy(), kc.cpu().numpy().astype(np.int64),
                            vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
     np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+
+
+def test_aggressive_decode_full_size(cuda_ready):
+    """The batch-sharded 8-bit workload at full size (B=32, 32 heads, S=16384, 3+3+2) through the
+    one-byte kernel; three batch rows against the oracle."""
+    from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
+    w = WORKLOADS["aggressive-332"]
+    q = make_quantizer(w)
+    kc, vc = make_kv_codes(w, q, DEV)
+    qv = make_query(w, DEV)
+    assert q.codec(torch.device(DEV)).describe(qv, kc, vc)["kernel"] == "attn_mha8_kernel"
+    out = decode_attention(q, qv, kc, vc)
+    p = oracle.QuantParams(dim=96, bits_z=3, bits_r=3, bits_theta=2, z_min=q.z_min, z_max=q.z_max, r_max=q.r_max)
+    rows = [0, 17, 31]
+    ref = oracle.attention(qv[rows].float().cpu().numpy(), kc[rows].cpu().numpy().astype(np.int64),
+                           vc[rows].cpu().numpy().astype(np.int64), q.R.numpy(), p)
+    np.testing.assert_allclose(out[rows].cpu().numpy(), ref, atol=TOL, rtol=0)
