@@ -1400,7 +1400,7 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
         pl.stages = mha8::STAGES;
         pl.smem = mha8::TOTAL;
         pl.chunk = 1 << 30;                // online softmax: no cap on the tokens of an item
-        pl.ctas_per_sm = 2;
+        pl.ctas_per_sm = 1;
     } else if (pl.mha12) {
         pl.TPL = 1;
         pl.tt = mha12::TT;
@@ -1440,8 +1440,8 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     const int64_t grid = (int64_t)num_sms() * pl.ctas_per_sm;
     // fixed cost of an item in tile units: the tensor-core kernel's items also rotate the group's
     // queries through global R and merge their splits, about eight of its 128-token tiles
-    // (query rotation, score table, warp merge and R reload: about three of the one-byte kernel's)
-    const double item_cost = pl.tc ? 8.0 : pl.mha8 ? 3.0 : 1.0;
+    // (query rotation, score table and warp merge: about two of the one-byte kernel's)
+    const double item_cost = pl.tc ? 8.0 : pl.mha8 ? 2.0 : 1.0;
     int best = 0;
     double best_cost = 1e300;
     const int min_split = a->num_splits > 0 ? a->num_splits : (tiles_total + max_tiles_item - 1) / max_tiles_item;

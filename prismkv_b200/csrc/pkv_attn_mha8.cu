@@ -2,14 +2,15 @@
 // (x, y) cells (at most 32 (r, theta) cells), uniform z bins, no BiasTable; one query
 // head per work unit (MHA, or grouped heads with every query head its own unit).
 //
-// One pass over an item's tokens.  The K and V codes of a 256-token tile arrive together
-// in one ring stage; each of the 8 consumer warps owns 32 tokens of every tile and keeps
-// its own running max, sum of weights and V accumulators (online softmax per warp); the
-// warps' states merge once per item, then finish_item normalises and applies R.
+// One CTA per SM, one pass over an item's tokens.  The K and V codes of a 512-token tile
+// arrive together in one ring stage; each of the 16 consumer warps owns 32 tokens of every
+// tile and keeps its own running max, sum of weights and V accumulators (online softmax per
+// warp, rescaled only when a warp vote sees a score above the running max); the warps'
+// states merge once per item, then finish_item normalises and applies R (resident in
+// shared memory for the CTA's lifetime).
 //
 //  * K: score table T[c][j] = q'_j . (z, x, y)(c) over all 256 byte values c and the 32
-//    triplets j (32 KB, over the R region), z and (x, y) straight from the codec's decode
-//    tables.  Lane l reads word l%8 of token 4s + l/8 (four codes) and takes the word's
+//    triplets j (32 KB), z and (x, y) straight from the codec's decode tables.  Lane l reads word l%8 of token 4s + l/8 (four codes) and takes the word's
 //    bytes starting at byte l/8, so the 32 table loads of a step hit 32 distinct banks.
 //    An 8-lane transpose-reduce completes 32 scores per 8 steps.
 //  * V: lane l reads 8 codes (triplets 8(l%4)..+7) of token l/4 of a group of 8 tokens.
@@ -23,18 +24,19 @@
 
 namespace pkv {
 namespace mha8 {
-constexpr int W = 8;                                   // consumer warps
-constexpr int TT = 256;                                // tokens per tile (32 per warp)
-constexpr int STAGES = 3;
+constexpr int W = 16;                                  // consumer warps (one CTA per SM)
+constexpr int TT = 32 * W;                             // tokens per tile (32 per warp)
+constexpr int STAGES = 4;
 constexpr int ROW = 32;                                // 32 one-byte codes per token
 constexpr int TILE = TT * ROW;                         // K (or V) codes of a tile
 constexpr int STAGE = 2 * TILE;                        // K then V
 constexpr int XY_ALIGN = 8192;                         // (r, theta) table: 32 rows x 256 bytes
 constexpr int OFF_XY = 0;
 constexpr int OFF_STAGE = OFF_XY + XY_ALIGN;
-constexpr int RBYTES = 96 * 96 * 4;                    // R, fp32, row pitch 96
-constexpr int OFF_RT = OFF_STAGE + STAGES * STAGE;     // R, or the [256][32] score table
-constexpr int OFF_Z = OFF_RT + RBYTES;                 // dec_z [<= 256]
+constexpr int RBYTES = 96 * 96 * 4;                    // R, fp32, row pitch 96, resident
+constexpr int OFF_R = OFF_STAGE + STAGES * STAGE;
+constexpr int OFF_KT = OFF_R + RBYTES;                 // [256][32] score table
+constexpr int OFF_Z = OFF_KT + 256 * 32 * 4;           // dec_z [<= 256]
 constexpr int OFF_Q = OFF_Z + 256 * 4;                 // [96] rotated query
 constexpr int OFF_QRAW = OFF_Q + 96 * 4;               // [96] raw query
 constexpr int OFF_ACC = OFF_QRAW + 96 * 4;             // [W][96] per-warp accumulators
@@ -45,8 +47,8 @@ constexpr int OFF_BAR = OFF_MISC + 16;                 // full[STAGES], empty[ST
 constexpr int LAYOUT = OFF_BAR + (2 * STAGES + 1) * 8;
 constexpr int TOTAL = LAYOUT + XY_ALIGN;               // slack to put the layout on an 8 KB boundary
 constexpr float MAGIC = 8388608.f;                     // 2^23
-static_assert(256 * 32 * 4 <= RBYTES, "score table must fit the R region");
-static_assert(OFF_STAGE % 128 == 0 && OFF_RT % 128 == 0 && OFF_BAR % 8 == 0, "alignment");
+static_assert(OFF_STAGE % 128 == 0 && OFF_R % 128 == 0 && OFF_KT % 128 == 0 && OFF_BAR % 8 == 0, "alignment");
+static_assert(TOTAL <= 227 * 1024, "shared memory of the one-byte attention kernel");
 }  // namespace mha8
 
 // 8-lane transpose-reduce within each group of 8 lanes: on exit v[0] of lane l holds the
@@ -64,14 +66,14 @@ __device__ __forceinline__ void transpose_reduce8(float (&v)[8], int lane) {
     }
 }
 
-__global__ void __launch_bounds__(mha8::W * 32 + 32, 2) attn_mha8_kernel(AttnParams p) {
+__global__ void __launch_bounds__(mha8::W * 32 + 32, 1) attn_mha8_kernel(AttnParams p) {
     using namespace mha8;
     extern __shared__ __align__(128) uint8_t mha8_smem[];
     // the (r, theta) table's row bits must be free in its base address: put the layout on 8 KB
     uint8_t* smem = mha8_smem + ((XY_ALIGN - ((uint32_t)__cvta_generic_to_shared(mha8_smem) & (XY_ALIGN - 1))) &
                                  (XY_ALIGN - 1));
-    float* kT = reinterpret_cast<float*>(smem + OFF_RT);       // score table, or R between uses
-    const float* sR = kT;
+    float* kT = reinterpret_cast<float*>(smem + OFF_KT);       // score table
+    float* sR = reinterpret_cast<float*>(smem + OFF_R);        // R, loaded once
     float* sXY = reinterpret_cast<float*>(smem + OFF_XY);
     float* sZ = reinterpret_cast<float*>(smem + OFF_Z);
     float* sQ = reinterpret_cast<float*>(smem + OFF_Q);
@@ -105,9 +107,9 @@ __global__ void __launch_bounds__(mha8::W * 32 + 32, 2) attn_mha8_kernel(AttnPar
         }
         mbar_init(rbar, 1);
         fence_mbar_init();
-        // R for the first item's query rotation, ahead of the code stream
+        // R, ahead of the code stream; it stays for every item's rotation and finish
         mbar_arrive_expect_tx(rbar, RBYTES);
-        bulk_g2s(kT, p.R, RBYTES, rbar);
+        bulk_g2s(sR, p.R, RBYTES, rbar);
     }
     float qreg = 0.f;                      // the first item's query, ahead of the code stream too
     {
@@ -138,15 +140,15 @@ __global__ void __launch_bounds__(mha8::W * 32 + 32, 2) attn_mha8_kernel(AttnPar
     const uint32_t fm = (uint32_t)(n_xy - 1) << 8;                      // flat cell bits at 8..
     const uint32_t zm = (uint32_t)(cz - 1) << (8 + bf);                 // z bits above them
     const float dzs = dz * exp2f((float)-(8 + bf));                     // per unit of the z field
-    int seq = 0, ruse = 0;
+    int seq = 0;
     bool alive = true;
+    if (!mbar_wait(rbar, 0, kErrWaitFull)) alive = false;               // R in place
     WorkCursor wc = work_begin(p);
     ItemRange r;
     while (work_next<false>(p, wc, r)) {
         const int ntok = r.tok1 - r.tok0;
         const int ntiles = (ntok + TT - 1) / TT;
         if (tid < 96) sQraw[tid] = qreg;
-        if (alive && !mbar_wait(rbar, ruse & 1, kErrWaitFull)) alive = false;   // R in place
         named_bar_sync(1, nthr);
         // q' = scale log2(e) R q: one warp per row, lanes over the input index
         {
@@ -161,15 +163,15 @@ __global__ void __launch_bounds__(mha8::W * 32 + 32, 2) attn_mha8_kernel(AttnPar
             }
         }
         named_bar_sync(1, nthr);
-        // score table over the R region: row c (byte value), column j (triplet); warp w
-        // fills rows w + 8k, lane j column j
+        // score table: row c (byte value), column j (triplet); warp w fills rows w + W k,
+        // lane j column j.  The previous item's last table reads are behind the barrier above.
         {
             const float qz = sQ[3 * lane], qx = sQ[3 * lane + 1], qy = sQ[3 * lane + 2];
             #pragma unroll 4
-            for (int k = 0; k < 32; ++k) {
-                const int c = (warp + 8 * k) & p.code_mask;
+            for (int k = 0; k < 256 / W; ++k) {
+                const int c = (warp + W * k) & p.code_mask;
                 const int fl = c & (n_xy - 1);
-                kT[(warp + 8 * k) * 32 + lane] = fmaf(qz, sZ[c >> bf], fmaf(qx, sXY[fl * 64], qy * sXY[fl * 64 + 1]));
+                kT[(warp + W * k) * 32 + lane] = fmaf(qz, sZ[c >> bf], fmaf(qx, sXY[fl * 64], qy * sXY[fl * 64 + 1]));
             }
         }
         named_bar_sync(1, nthr);
@@ -200,10 +202,10 @@ __global__ void __launch_bounds__(mha8::W * 32 + 32, 2) attn_mha8_kernel(AttnPar
                 transpose_reduce8(ps, lane);
                 const int tokk = warp * 32 + 4 * ki + kg;             // token of ps[0]
                 const float sc = (tokk < nt) ? ps[0] : -INFINITY;
-                float mt = sc;
-                #pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-                if (mt > mrun) {                                      // warp-uniform
+                if (__any_sync(0xffffffffu, sc > mrun)) {             // rare after the first tiles
+                    float mt = sc;
+                    #pragma unroll
+                    for (int off = 16; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
                     const float f = fast_exp2(mrun - mt);             // 0 on the first valid tile
                     lsum *= f;
                     #pragma unroll
@@ -242,14 +244,6 @@ __global__ void __launch_bounds__(mha8::W * 32 + 32, 2) attn_mha8_kernel(AttnPar
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        // every warp is past its last table read: bring R back for the finish and the next rotation
-        named_bar_sync(1, nthr);
-        if (tid == 0) {
-            fence_proxy_async_smem();
-            mbar_arrive_expect_tx(rbar, RBYTES);
-            bulk_g2s(kT, p.R, RBYTES, rbar);
-        }
-        ++ruse;
         {                                                  // prefetch the next item's query
             WorkCursor pc = wc;
             ItemRange rn;
@@ -304,12 +298,11 @@ __global__ void __launch_bounds__(mha8::W * 32 + 32, 2) attn_mha8_kernel(AttnPar
                 sL[0] = L;
             }
         }
-        if (alive && !mbar_wait(rbar, ruse & 1, kErrWaitFull)) alive = false;   // R back in place
         named_bar_sync(1, nthr);
-        finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 1);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 4);
     }
-    // the last R copy must land before the CTA exits
-    if (tid == 0 && alive) mbar_wait(rbar, ruse & 1, kErrWaitDrain);
+    // a copy of R that never landed must not outlive the CTA
+    if (tid == 0 && !alive) mbar_wait(rbar, 0, kErrWaitDrain);
 }
 
 }  // namespace pkv
