@@ -183,7 +183,8 @@ PKV_API int pkv_attn_decode(const pkv_codec *c, const pkv_attn_args *a,
 /* Which kernel and split plan pkv_attn_decode would use for these arguments
  * (introspection for tests and benchmarks; launches nothing; the output
  * pointers of `a` may be null).                                           */
-enum { PKV_KERNEL_MHA12 = 1, PKV_KERNEL_POLAR = 2, PKV_KERNEL_LUT = 3, PKV_KERNEL_TC = 4, PKV_KERNEL_MHA8 = 5 };
+enum { PKV_KERNEL_MHA12 = 1, PKV_KERNEL_POLAR = 2, PKV_KERNEL_LUT = 3, PKV_KERNEL_TC = 4, PKV_KERNEL_MHA8 = 5,
+       PKV_KERNEL_MHA12_STREAM = 6 };
 typedef struct pkv_attn_plan {
     int32_t kernel;            /* PKV_KERNEL_*                                  */
     int32_t num_splits;        /* sequence splits per (batch, kv head)          */

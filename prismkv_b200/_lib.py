@@ -54,7 +54,7 @@ class PkvAttnPlan(ctypes.Structure):
 
 
 KERNEL_NAMES = {1: "attn_mha12_kernel", 2: "attn_polar_kernel", 3: "attn_lut_kernel", 4: "attn_tc_kernel",
-                5: "attn_mha8_kernel"}
+                5: "attn_mha8_kernel", 6: "attn_mha12_stream_kernel"}
 
 _lock = threading.Lock()
 _lib = None

@@ -98,6 +98,10 @@ CASES = [
     (2, 8, 4, 2000, "v1", (4, 4, 4), torch.float32, 2),
     (2, 8, 4, 2000, "v1", (4, 4, 4), torch.float32, 7),
     (2, 8, 4, 2000, "v1", (4, 4, 4), torch.float32, 16),
+    (1, 8, 8, 5000, "v1", (4, 4, 4), torch.float32, 0),           # past 4096 tokens: one-pass 12-bit kernel
+    (2, 8, 8, 4097, "v1", (4, 4, 4), torch.bfloat16, 0),
+    (1, 32, 8, 9000, "v1", (4, 4, 4), torch.float32, 0),          # grouped, one query head per unit
+    (1, 8, 8, 12345, "v1", (4, 4, 4), torch.float16, 5),
 ]
 
 
@@ -126,12 +130,12 @@ def test_attention_other_head_dims(cuda_ready, dim):
     np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
 
 
-@pytest.mark.parametrize("bits", [(4, 4, 4), (3, 3, 2)])
-def test_attention_ragged_and_empty_rows(cuda_ready, bits):
+@pytest.mark.parametrize("bits,S", [((4, 4, 4), 512), ((3, 3, 2), 512), ((4, 4, 4), 6000)])
+def test_attention_ragged_and_empty_rows(cuda_ready, bits, S):
     q, p = _setup("v1", bits)
-    kc, vc = _codes(q, 3, 8, 512, seed=2)
+    kc, vc = _codes(q, 3, 8, S, seed=2)
     qv = torch.randn(3, 8, 96, generator=torch.Generator(device=DEV).manual_seed(2), device=DEV)
-    lens = torch.tensor([512, 0, 77], dtype=torch.int32, device=DEV)
+    lens = torch.tensor([S, 0, 77 if S < 1000 else 4500], dtype=torch.int32, device=DEV)
     for splits in (0, 1, 3):
         out = decode_attention(q, qv, kc, vc, seq_lens=lens, num_splits=splits)
         ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64), vc.cpu().numpy().astype(np.int64),
@@ -215,6 +219,8 @@ def test_attention_shapes_in_turn_share_workspace(cuda_ready):
 @pytest.mark.parametrize("B,Hq,Hkv,S,variant,bits,kernel", [
     (8, 32, 32, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),
     (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),        # grouped heads, one query head per unit
+    (1, 8, 8, 4097, "v1", (4, 4, 4), "attn_mha12_stream_kernel"),
+    (4, 32, 8, 131072, "v1", (4, 4, 4), "attn_mha12_stream_kernel"),
     (2, 8, 8, 4096, "v1", (3, 3, 2), "attn_mha8_kernel"),
     (2, 32, 8, 4096, "v1", (3, 3, 2), "attn_mha8_kernel"),        # fp32 queries of a group
     (2, 8, 8, 4096, "v1", (2, 3, 3), "attn_polar_kernel"),
