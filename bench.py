@@ -207,6 +207,8 @@ def bench_decode(args, ws, rank, device):
     from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
 
     w = WORKLOADS[args.workload]
+    if args.batch:
+        w = w.scaled(batch=args.batch)         # a smaller case of the same kernel, for profilers
     mode, lw, span = _partition(w, ws, rank)
     quant = make_quantizer(w)
     codec = quant.codec(device)
@@ -355,7 +357,8 @@ def bench_decode(args, ws, rank, device):
                    "parallelism": parallelism},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": _committed_traffic(plan["kernel"], w.name) if mode == "replicas" else None,
+                     "traffic": (_committed_traffic(plan["kernel"], w.name)
+                                 if mode == "replicas" and not args.batch else None),
                      "kernel": plan["kernel"], "num_splits": plan["num_splits"],
                      "balanced": bool(plan["balanced"])},
         "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
@@ -532,6 +535,8 @@ def main(argv=None):
     ap.add_argument("--mode", default="decode", choices=["decode", "encode"])
     ap.add_argument("--encode-workload", default="learned-gqa", choices=["learned-gqa", "phi3-decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="decode: override the workload's batch (small cases for ncu captures)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="split-sequence exchange: symmetric-memory peer reads or an NCCL all-gather")
     args = ap.parse_args(argv)
