@@ -36,23 +36,30 @@ __host__ __device__ constexpr int threads_for(int gm) { return (2 + SM_WARPS + d
 constexpr int STAGE = 2 * TT * 64;         // 16 KB: K and V codes, 12-bit in uint16
 constexpr int HCHUNK = TT * 64;            // 8 KB: one 32-column chunk of a decoded tile
 constexpr int KH = 3 * HCHUNK;             // Khat tile
-constexpr int VH = 4 * HCHUNK;             // Vhat tile, chunk 3 (rows 96..127 of the MMA) zero
+// Vhat tiles: 3 chunks each, 24 KB apart.  The PV MMA reads 4 chunks (M = 128 rows): chunk 3 of
+// buffer b is chunk 0 of buffer b + 1 (or the zeroed tail after the last one), so output rows
+// 96..127 are unused garbage and need no zero padding.
+constexpr int NVH = 3;                     // Vhat buffers
+constexpr int VHS = 3 * HCHUNK;            // stride between Vhat buffers
+constexpr int VH_REGION = NVH * VHS + HCHUNK;
 constexpr int PCH = NG * 64;               // 1 KB: P chunk of 32 tokens x 16 heads
 constexpr int PT = 4 * PCH;
 constexpr int QB = 3 * NG * 64;            // q' operand: 3 chunks of 16 rows
 constexpr int OFF_STAGE = 0;
 constexpr int OFF_KH = OFF_STAGE + STAGES * STAGE;
 constexpr int OFF_VH = OFF_KH + 2 * KH;
-constexpr int OFF_P = OFF_VH + 2 * VH;
+constexpr int OFF_P = OFF_VH + VH_REGION;
 constexpr int OFF_QB = OFF_P + 2 * PT;
-constexpr int OFF_LUTZ = OFF_QB + QB;                       // dec_z [<= 256]
-constexpr int OFF_LUTXY = OFF_LUTZ + 256 * 4;               // dec_xy [<= 4096] float2
-constexpr int LUTXY_BYTES = 4096 * 8;
+// decode tables already rounded to the operand type: z as one 16-bit value, (x, y) as a packed
+// pair, so a code costs two loads and no conversion
+constexpr int OFF_LUTZ = OFF_QB + QB;                       // dec_z [<= 256] bf16 / f16
+constexpr int OFF_LUTXY = OFF_LUTZ + 256 * 2;               // dec_xy [<= 4096] bf16x2 / f16x2
+constexpr int LUTXY_BYTES = 4096 * 4;
 constexpr int OFF_M = OFF_LUTXY + LUTXY_BYTES;              // sM, sL [NG], alpha [2][NG], red [4][NG], flag
 constexpr int OFF_O = OFF_M + (2 * NG + 2 * NG + SM_WARPS * NG) * 4 + 16;   // sO [NG][96] (finish_item)
 constexpr int OFF_FIN = OFF_O + NG * D * 4;                 // sFin [NG][96]; raw queries before the finish
 constexpr int OFF_BAR = OFF_FIN + NG * D * 4 + 16;
-constexpr int NBAR = 2 * STAGES + 2 * 10 + 1;
+constexpr int NBAR = 2 * STAGES + 2 * 8 + 2 * NVH + 1;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory of the tensor-core attention kernel");
@@ -128,8 +135,8 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
     // offset) so that every access below stays a shared-memory access
     uint8_t* smem = atc_smem_raw + ((1024u - (smem_u32(atc_smem_raw) & 1023u)) & 1023u);
     const uint32_t sb = smem_u32(smem);
-    float* lutz = reinterpret_cast<float*>(smem + OFF_LUTZ);
-    float2* lutxy = reinterpret_cast<float2*>(smem + OFF_LUTXY);
+    uint16_t* lutz = reinterpret_cast<uint16_t*>(smem + OFF_LUTZ);
+    uint32_t* lutxy = reinterpret_cast<uint32_t*>(smem + OFF_LUTXY);
     float* sM = reinterpret_cast<float*>(smem + OFF_M);
     float* sL = sM + NG;
     float* sAlpha = sL + NG;                 // [2][NG]
@@ -143,9 +150,9 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
     uint64_t* empty = full + STAGES;         // [STAGES] codes consumed (decoder warps)
     uint64_t* kh_full = empty + STAGES;      // [2]
     uint64_t* kh_empty = kh_full + 2;        // [2] scores MMA done with Khat
-    uint64_t* vh_full = kh_empty + 2;
-    uint64_t* vh_empty = vh_full + 2;        // [2] PV MMA done with Vhat
-    uint64_t* s_full = vh_empty + 2;         // [2] scores in TMEM
+    uint64_t* vh_full = kh_empty + 2;        // [NVH]
+    uint64_t* vh_empty = vh_full + NVH;      // [NVH] PV MMA done with Vhat
+    uint64_t* s_full = vh_empty + NVH;       // [2] scores in TMEM
     uint64_t* s_empty = s_full + 2;          // [2] softmax read them
     uint64_t* p_full = s_empty + 2;          // [2] P in shared memory
     uint64_t* p_empty = p_full + 2;          // [2] PV MMA done with P
@@ -161,11 +168,13 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
     const uint32_t cmask = (uint32_t)p.code_mask, fmask = (uint32_t)p.flat_mask;
 
     // ---- set-up: LUTs, zero padding of the operands, barriers, tensor memory ----
-    for (int i = tid; i < p.Cz; i += THREADS) lutz[i] = __ldg(p.dec_z + i);
-    for (int i = tid; i < p.n_xy; i += THREADS) lutxy[i] = __ldg(reinterpret_cast<const float2*>(p.dec_xy) + i);
-    for (int i = tid; i < (2 * VH) / 16; i += THREADS) {          // Vhat chunk 3 and everything else: zero
-        reinterpret_cast<uint4*>(smem + OFF_VH)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < p.Cz; i += THREADS) lutz[i] = half1(__ldg(p.dec_z + i), f16);
+    for (int i = tid; i < p.n_xy; i += THREADS) {
+        const float2 xy = __ldg(reinterpret_cast<const float2*>(p.dec_xy) + i);
+        lutxy[i] = pack2(xy.x, xy.y, f16);
     }
+    for (int i = tid; i < VH_REGION / 16; i += THREADS)           // Vhat tiles and the tail: finite
+        reinterpret_cast<uint4*>(smem + OFF_VH)[i] = make_uint4(0, 0, 0, 0);
     for (int i = tid; i < (2 * PT + QB) / 16; i += THREADS)
         reinterpret_cast<uint4*>(smem + OFF_P)[i] = make_uint4(0, 0, 0, 0);
     if (tid == 0) {
@@ -173,11 +182,13 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], DEC_WARPS);
         }
+        for (int b = 0; b < NVH; ++b) {
+            mbar_init(&vh_full[b], DEC_WARPS);
+            mbar_init(&vh_empty[b], 1);
+        }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&kh_full[b], DEC_WARPS);
             mbar_init(&kh_empty[b], 1);
-            mbar_init(&vh_full[b], DEC_WARPS);
-            mbar_init(&vh_empty[b], 1);
             mbar_init(&s_full[b], 1);
             mbar_init(&s_empty[b], SM_WARPS);
             mbar_init(&p_full[b], SM_WARPS);
@@ -224,17 +235,17 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
                 etc::mma_commit(smem_u32(&s_full[b]));
             };
             auto pv = [&](int t) {
-                const int b = t & 1;
+                const int b = t & 1, b3 = t % NVH;
                 if (alive && !mbar_wait_spin(&p_full[b], (t >> 1) & 1, kErrWaitFull)) alive = false;
-                if (alive && !mbar_wait_spin(&vh_full[b], (t >> 1) & 1, kErrWaitFull)) alive = false;
+                if (alive && !mbar_wait_spin(&vh_full[b3], (t / NVH) & 1, kErrWaitFull)) alive = false;
                 if (alive && t >= 2 && !mbar_wait_spin(&o_empty[b], ((t >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
                 if (!alive) return;
                 etc::tc_fence_after();
                 #pragma unroll
                 for (int k = 0; k < TT / 16; ++k)
-                    mma(tmem + (uint32_t)(32 + b * NG), desc_mn(sb + OFF_VH + b * VH + k * 1024),
+                    mma(tmem + (uint32_t)(32 + b * NG), desc_mn(sb + OFF_VH + b3 * VHS + k * 1024),
                         desc_k(sb + OFF_P + b * PT + (k >> 1) * PCH + (k & 1) * 32), id_o, k != 0);
-                etc::mma_commit(smem_u32(&vh_empty[b]));
+                etc::mma_commit(smem_u32(&vh_empty[b3]));
                 etc::mma_commit(smem_u32(&p_empty[b]));
                 etc::mma_commit(smem_u32(&o_full[b]));
             };
@@ -263,23 +274,30 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
         while (work_next<false>(p, wc, r)) {
             const int nt = (r.tok1 - r.tok0 + TT - 1) / TT;
             for (int j = 0; j < nt; ++j, ++it, ++seq) {
-                const int s = seq % STAGES, b = it & 1;
+                const int s = seq % STAGES, b = it & 1, b3 = it % NVH;
                 if (alive && !mbar_wait_spin(&full[s], (seq / STAGES) & 1, kErrWaitFull)) alive = false;
-                if (alive && it >= 2 && !mbar_wait_spin(&kh_empty[b], ((it >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
-                if (alive && it >= 2 && !mbar_wait_spin(&vh_empty[b], ((it >> 1) - 1) & 1, kErrWaitEmpty)) alive = false;
-                if (alive) {
-                    const uint8_t* stage = smem + OFF_STAGE + s * STAGE;
-                    // thread -> (token t0 + i * TSTEP, triplet pair jp); the swizzle key (t >> 1) & 3 is the
-                    // same for all its tokens (TSTEP is a multiple of 8), so the three store offsets are
-                    // fixed and advance by TSTEP rows per step
-                    constexpr int NTH = DEC_WARPS * 32, TSTEP = NTH / 16;
-                    const int jp = dt & 15, t0 = dt >> 4;
-                    const uint32_t o0 = sw_off(t0, 6 * jp, HCHUNK), o1 = sw_off(t0, 6 * jp + 2, HCHUNK),
-                                   o2 = sw_off(t0, 6 * jp + 4, HCHUNK);
-                    #pragma unroll 1
-                    for (int kv = 0; kv < 2; ++kv) {
+                // thread -> (token t0 + i * TSTEP, triplet pair jp); the swizzle key (t >> 1) & 3 is the
+                // same for all its tokens (TSTEP is a multiple of 8), so the three store offsets are
+                // fixed and advance by TSTEP rows per step
+                constexpr int NTH = DEC_WARPS * 32, TSTEP = NTH / 16;
+                const int jp = dt & 15, t0 = dt >> 4;
+                const uint32_t o0 = sw_off(t0, 6 * jp, HCHUNK), o1 = sw_off(t0, 6 * jp + 2, HCHUNK),
+                               o2 = sw_off(t0, 6 * jp + 4, HCHUNK);
+                const uint8_t* stage = smem + OFF_STAGE + s * STAGE;
+                // K first (its buffer frees as soon as the scores MMA is done), then V (its buffer
+                // frees only after the PV MMA of the tile NVH back)
+                #pragma unroll 1
+                for (int kv = 0; kv < 2; ++kv) {
+                    if (kv == 0) {
+                        if (alive && it >= 2 && !mbar_wait_spin(&kh_empty[b], ((it >> 1) - 1) & 1, kErrWaitEmpty))
+                            alive = false;
+                    } else {
+                        if (alive && it >= NVH && !mbar_wait_spin(&vh_empty[b3], ((it / NVH) - 1) & 1, kErrWaitEmpty))
+                            alive = false;
+                    }
+                    if (alive) {
                         const uint8_t* codes = stage + kv * TT * 32 * CB + t0 * 32 * CB + jp * 2 * CB;
-                        uint8_t* dst = smem + (kv == 0 ? OFF_KH + b * KH : OFF_VH + b * VH);
+                        uint8_t* dst = smem + (kv == 0 ? OFF_KH + b * KH : OFF_VH + b3 * VHS);
                         #pragma unroll
                         for (int i = 0; i < TT / TSTEP; ++i) {
                             uint32_t c0, c1;
@@ -294,23 +312,21 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
                             }
                             c0 &= cmask;
                             c1 &= cmask;
-                            const float z0 = lutz[c0 >> bf], z1 = lutz[c1 >> bf];
-                            const float2 xy0 = lutxy[p.xy_per_z ? c0 : (c0 & fmask)];
-                            const float2 xy1 = lutxy[p.xy_per_z ? c1 : (c1 & fmask)];
+                            const uint32_t z0 = lutz[c0 >> bf], z1 = lutz[c1 >> bf];
+                            const uint32_t xy0 = lutxy[p.xy_per_z ? c0 : (c0 & fmask)];
+                            const uint32_t xy1 = lutxy[p.xy_per_z ? c1 : (c1 & fmask)];
                             uint8_t* d = dst + i * TSTEP * 64;
-                            *reinterpret_cast<uint32_t*>(d + o0) = pack2(z0, xy0.x, f16);
-                            *reinterpret_cast<uint32_t*>(d + o1) = pack2(xy0.y, z1, f16);
-                            *reinterpret_cast<uint32_t*>(d + o2) = pack2(xy1.x, xy1.y, f16);
+                            // dims 6jp .. 6jp+5 = z0 x0 | y0 z1 | x1 y1
+                            *reinterpret_cast<uint32_t*>(d + o0) = __byte_perm(z0, xy0, 0x5410);
+                            *reinterpret_cast<uint32_t*>(d + o1) = __byte_perm(xy0, z1, 0x5432);
+                            *reinterpret_cast<uint32_t*>(d + o2) = xy1;
                         }
+                        fence_proxy_async_smem();             // generic stores -> tensor-core reads
                     }
-                    fence_proxy_async_smem();                 // generic stores -> tensor-core reads
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(kv == 0 ? &kh_full[b] : &vh_full[b3]);
                 }
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&empty[s]);
-                    mbar_arrive(&kh_full[b]);
-                    mbar_arrive(&vh_full[b]);
-                }
+                if (lane == 0) mbar_arrive(&empty[s]);
             }
         }
     } else {
