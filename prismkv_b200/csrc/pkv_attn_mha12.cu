@@ -382,6 +382,10 @@ __global__ void __launch_bounds__(mha12s::W * 32 + 32, 2) attn_mha12_stream_kern
     uint64_t* empty = full + STAGES;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // R (36 KB) is read from global memory by every item's rotation and finish; once the code
+    // stream runs, a miss on it waits behind the bulk copies, so bring it into L2 first
+    constexpr int R_LINES = 96 * 96 * 4 / 128;
+    for (int i = tid; i < R_LINES; i += blockDim.x) prefetch_l2(p.R + i * 32);
     const float dr = p.r_max / 15.f;
     const float z0 = __ldg(p.dec_z), dz = __ldg(p.dec_z + 1) - z0;     // uniform z bins: z = z0 + i dz
 
@@ -476,6 +480,8 @@ __global__ void __launch_bounds__(mha12s::W * 32 + 32, 2) attn_mha12_stream_kern
         #pragma unroll
         for (int k = 0; k < 8; ++k) axy[k] = make_float2(0.f, 0.f);
         for (int tile = 0; tile < ntiles; ++tile, ++seq) {
+            if (tile + 1 == ntiles)                      // the finish and the next rotation read R
+                for (int i = tid; i < R_LINES; i += nthr) prefetch_l2(p.R + i * 32);
             const int s = seq % STAGES;
             if (alive && !mbar_wait(&full[s], (seq / STAGES) & 1, kErrWaitFull)) alive = false;
             const int nt = min(TT, ntok - tile * TT);

@@ -162,6 +162,10 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // R (36 KB) is read from global memory by the query rotation and the finish; once the code
+    // stream runs, a miss on it waits behind the bulk copies, so bring it into L2 first
+    constexpr int R_LINES = D * D * 4 / 128;
+    for (int i = tid; i < R_LINES; i += THREADS) prefetch_l2(p.R + i * 32);
     const bool f16 = (p.qdt == PKV_F16);
     const uint32_t ab = f16 ? 0u : 1u;
     const int bf = p.bits_flat;
@@ -353,17 +357,34 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
                     sQs[idx] = q_load(p.q, p.qdt, (int64_t)r.b * p.q_bs + (int64_t)(r.hk * G + g) * p.q_hs + i);
                 }
                 named_bar_sync(1, nthr);
-                for (int idx = gt; idx < G * D; idx += nthr) {
-                    const int g = idx / D, k = idx % D;
-                    const float* Rk = p.R + k * D;
-                    float v0 = 0.f, v1 = 0.f;
-                    #pragma unroll 8
-                    for (int i = 0; i < D; i += 2) {
-                        v0 = fmaf(__ldg(Rk + i), sQs[g * D + i], v0);
-                        v1 = fmaf(__ldg(Rk + i + 1), sQs[g * D + i + 1], v1);
+                // one warp per row k of R, lanes over the input index: each row is three coalesced
+                // 128-byte loads from L2, shared by the group's heads; six rows' loads are in
+                // flight at once, so the 24 rows of a warp cost four memory round trips
+                constexpr int RB = 6, ROWS = D / SM_WARPS;
+                static_assert(ROWS % RB == 0, "rows per batch");
+                for (int k0 = 0; k0 < ROWS; k0 += RB) {
+                    float rv[RB][3];
+                    #pragma unroll
+                    for (int u = 0; u < RB; ++u) {
+                        const float* Rk = p.R + (quarter + SM_WARPS * (k0 + u)) * D;
+                        rv[u][0] = __ldg(Rk + lane);
+                        rv[u][1] = __ldg(Rk + lane + 32);
+                        rv[u][2] = __ldg(Rk + lane + 64);
                     }
-                    *reinterpret_cast<uint16_t*>(smem + OFF_QB + sw_off(g, k, NG * 64)) =
-                        half1((v0 + v1) * p.scale_log2, f16);
+                    for (int g = 0; g < G; ++g) {
+                        const float* qg = sQs + g * D;
+                        const float qa = qg[lane], qb = qg[lane + 32], qc = qg[lane + 64];
+                        #pragma unroll
+                        for (int u = 0; u < RB; ++u) {
+                            float v = fmaf(rv[u][0], qa, fmaf(rv[u][1], qb, rv[u][2] * qc));
+                            #pragma unroll
+                            for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                            if (lane == 0)
+                                *reinterpret_cast<uint16_t*>(smem + OFF_QB +
+                                                             sw_off(g, quarter + SM_WARPS * (k0 + u), NG * 64)) =
+                                    half1(v * p.scale_log2, f16);
+                        }
+                    }
                 }
                 fence_proxy_async_smem();
                 named_bar_sync(1, nthr);
@@ -371,6 +392,8 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
                 ++items;
             }
             for (int j = 0; j <= nt; ++j) {
+                if (j + 1 == nt)                         // the finish reads R: back into L2
+                    for (int i = gt; i < R_LINES; i += nthr) prefetch_l2(p.R + i * 32);
                 // ---- softmax of tile j ----
                 if (j < nt) {
                     const int t = it + j, b = t & 1;

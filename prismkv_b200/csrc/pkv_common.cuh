@@ -187,6 +187,11 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
 // dst, src 16-byte aligned; bytes a multiple of 16.
+// Pull one 128-byte line into L2 ahead of its use (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+    asm volatile("prefetch.global.L2 [%0];" :: "l"(ptr));
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
