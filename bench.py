@@ -342,7 +342,9 @@ def bench_decode(args, ws, rank, device):
     d2h = h_out.numel() * h_out.element_size()
 
     parallelism = {"replicas": f"replicas x{ws}", "batch": f"batch-sharded x{ws} (no collective)",
-                   "sequence": f"sequence-sharded x{ws} (NCCL all-gather of partials + LSE combine)"}[mode]
+                   "sequence": f"sequence-sharded x{ws} (" + ("symmetric-memory peer reads" if exchange is not None
+                                                                else "NCCL all-gather") +
+                               " of partials + LSE combine)"}[mode]
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
