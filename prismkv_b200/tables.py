@@ -182,7 +182,7 @@ def dec_xy_polar(r_max: float, bits_r: int, bits_theta: int) -> np.ndarray:
     return np.stack([(r_q * c).astype(F32), (r_q * s).astype(F32)], axis=-1)
 
 
-CELL_GRID = 64          # cells per axis of the nearest-centroid candidate grid
+CELL_GRID = 128         # cells per axis of the nearest-centroid candidate grid
 CELL_MAX = 16           # candidates kept per cell; fuller cells fall back to the full scan
 
 

@@ -13,6 +13,7 @@ import oracle
 from conftest import golden_files, load_golden, params_from, quantizer_from
 from prismkv_b200 import StackedPlaneQuantizer, LearnedSliceCodebook, BiasTable, LloydMaxQuantizer1D
 from prismkv_b200.synthetic import synthetic_bias, synthetic_codebook
+from prismkv_b200 import tables
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -189,13 +190,14 @@ def test_learned_encode_candidate_cells_equal_full_scan(cuda_ready, bits):
     points at all scales (inside, at the edge of and beyond the cell grid) and on cell edges."""
     q = _quantizer("learned", bits)
     codec = q.codec(torch.device(DEV))
-    assert codec.struct.cell_grid == 64
+    assert codec.struct.cell_grid == tables.CELL_GRID
     g = torch.Generator().manual_seed(77)
     parts = [torch.randn(20000, 96, generator=g) * s for s in (0.3, 1.0, 3.0, 8.0)]
     # rows whose rotated (x, y) land exactly on cell edges: rotate grid points back with R
     edge = torch.zeros(4096, 96)
-    w = 2 * q.r_max / 64
-    vals = (torch.randint(-32, 33, (4096, 64), generator=g).float() * w).reshape(4096, 64)
+    G = tables.CELL_GRID
+    w = 2 * q.r_max / G
+    vals = (torch.randint(-G // 2, G // 2 + 1, (4096, 64), generator=g).float() * w).reshape(4096, 64)
     rot = torch.zeros(4096, 96)
     rot[:, 1::3] = vals[:, :32]
     rot[:, 2::3] = vals[:, 32:]
