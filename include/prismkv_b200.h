@@ -97,7 +97,8 @@ typedef struct pkv_codec {
     /* Learned codebooks, optional: candidate centroids per cell of a
      * cell_grid x cell_grid grid over [-cell_half_width, cell_half_width]^2
      * per z-bin (cell_idx [2^bits_z][grid][grid][16] ascending indices,
-     * cell_cnt [2^bits_z][grid][grid], 255 = scan all).  NULL: full scan.  */
+     * cell_cnt [2^bits_z][grid][grid], 255 = scan all).  NULL, or a
+     * cell_idx that is not 16-byte aligned: full scan.                       */
     const uint8_t *cell_idx;
     const uint8_t *cell_cnt;
     int32_t cell_grid;

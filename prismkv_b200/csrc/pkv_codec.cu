@@ -127,15 +127,22 @@ __device__ __forceinline__ int nearest_centroid_cells(const CodecArgs& a, int iz
             const int cell = (iz * a.cell_grid + (int)fy) * a.cell_grid + (int)fx;
             const int n = __ldg(a.cell_cnt + cell);
             if (n <= kCellMax) {
-                const uint8_t* cand = a.cell_idx + (size_t)cell * kCellMax;
+                // the cell's candidate list is one 16-byte row: a single load, then the scan in
+                // list (ascending index) order with a strict compare keeps the first minimum
+                static_assert(kCellMax == 16, "one 16-byte row per cell");
+                const uint4 row = __ldg(reinterpret_cast<const uint4*>(a.cell_idx) + cell);
+                const uint32_t w4[4] = {row.x, row.y, row.z, row.w};
                 float best = INFINITY;
                 int bi = 0;
-                for (int i = 0; i < n; ++i) {
-                    const int k = __ldg(cand + i);
-                    const float2 c = cb_fast[k];
-                    const float dx = x - c.x, dy = y - c.y;
-                    const float d2 = fmaf(dx, dx, dy * dy);
-                    if (d2 < best) { best = d2; bi = k; }
+                #pragma unroll
+                for (int i = 0; i < kCellMax; ++i) {
+                    if (i < n) {
+                        const int k = (int)((w4[i >> 2] >> (8 * (i & 3))) & 0xFFu);
+                        const float2 c = cb_fast[k];
+                        const float dx = x - c.x, dy = y - c.y;
+                        const float d2 = fmaf(dx, dx, dy * dy);
+                        if (d2 < best) { best = d2; bi = k; }
+                    }
                 }
                 return bi;
             }
@@ -412,8 +419,10 @@ static void fill_args(CodecArgs& a, const pkv_codec* c) {
     a.R = c->R; a.z_thr = c->z_thr; a.r2_thr = c->r2_thr; a.th_thr = c->th_thr;
     a.codebook = c->codebook; a.dec_z = c->dec_z; a.dec_xy = c->dec_xy;
     a.cell_grid = 0;
+    // each cell's 16-entry candidate row is read with one 16-byte load: a table that is not
+    // 16-byte aligned takes the full scan instead
     if (c->xy_mode == 1 && c->cell_idx && c->cell_cnt && c->cell_grid > 0 && c->cell_half_width > 0.f &&
-        (1 << (c->bits_r + c->bits_theta)) <= 256) {
+        (reinterpret_cast<uintptr_t>(c->cell_idx) & 15u) == 0 && (1 << (c->bits_r + c->bits_theta)) <= 256) {
         a.cell_idx = c->cell_idx;
         a.cell_cnt = c->cell_cnt;
         a.cell_grid = c->cell_grid;
