@@ -11,23 +11,31 @@
 //
 // Common schedule:
 //  * codes: (B, Hkv, S, m) of uint8/uint16, one m-code row per token;
-//  * one work item = (b, kv head, split) = a contiguous token range;
-//    persistent CTAs take items round-robin;
+//  * one work item = (b, unit head, split) = a contiguous token range (the
+//    unit head is the KV head, or the query head for grouped heads on the
+//    one-head kernels); persistent CTAs take items round-robin, or balanced
+//    tile ranges (the one-pass LUT kernel);
 //  * a producer warp streams code tiles into a shared-memory ring with 1-D
-//    TMA bulk copies completing on mbarriers; consumer warps own 32 tokens of
-//    a tile each, lane j owning triplet j;
-//  * splits of one (b, kv head) write (m, l, o) partials to the workspace;
-//    the last CTA to finish (atomic counter) merges them, normalises and
-//    applies R once, then resets the counter.
+//    TMA bulk copies completing on mbarriers;
+//  * splits of one unit write (m, l, o) partials to the workspace; the last
+//    CTA to finish (atomic counter) merges them, normalises and applies R
+//    once, then resets the counter.
 //
-// Two kernels:
-//  * attn_polar_kernel -- uniform polar (x, y) bins (any z bins, optional
-//    BiasTable): two passes per item (K -> scores in shared memory, exact
-//    max, then V with fixed weights).  K scores come from per-lane tables
-//    indexed by the code fields (one bank per lane: conflict-free), V from a
-//    16-entry (cos, sin) table and the radius index itself.
-//  * attn_lut_kernel -- any codec (learned codebooks): one pass, online
-//    softmax, (z, x, y) from full-code LUTs.
+// Kernels (plan_attn below picks one per call):
+//  * attn_polar_kernel (this file) -- uniform polar (x, y) bins (any z bins,
+//    optional BiasTable): two passes per item (K -> scores in shared memory,
+//    exact max, then V with fixed weights).  K scores come from per-lane
+//    tables indexed by the code fields (one bank per lane: conflict-free), V
+//    from a 16-entry (cos, sin) table and the radius index itself.
+//  * attn_lut_kernel (this file) -- any codec (learned codebooks): one pass,
+//    online softmax, (z, x, y) from full-code LUTs.
+//  * attn_mha12_kernel, attn_mha12_stream_kernel (pkv_attn_mha12.cu) -- the
+//    12-bit uniform-polar head_dim-96 case, one query head per unit: two
+//    passes for sequences of one 4096-token item, one pass beyond.
+//  * attn_mha8_kernel (pkv_attn_mha8.cu) -- one-byte uniform-polar codes,
+//    head_dim 96, one query head per unit.
+//  * attn_tc_kernel (pkv_attn_tc.cu) -- tcgen05 tensor cores for bf16/fp16
+//    queries of grouped heads or per-z-bin tables.
 //
 // Every mbarrier wait is bounded; on expiry the kernel sets the device error
 // word, stops issuing copies, drains what it issued and returns.
