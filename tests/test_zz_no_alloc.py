@@ -46,10 +46,12 @@ def _workspace_bytes(codec, a):
 
 CASES = [
     # B, Hq, Hkv, S, bits, qdtype, splits
-    (2, 8, 8, 16384, (4, 4, 4), torch.bfloat16, 0),    # 12-bit MHA kernel, >= 4 splits per head
-    (1, 32, 8, 9000, (4, 4, 4), torch.float32, 0),     # GQA, polar kernel
-    (2, 4, 4, 3000, (2, 3, 3), torch.float16, 6),      # 8-bit codes, forced splits
-    (1, 8, 8, 777, (4, 4, 4), torch.float32, 3),       # ragged last split
+    (2, 8, 8, 16384, (4, 4, 4), torch.bfloat16, 0),    # 12-bit one-pass kernel, planner's splits
+    (1, 32, 8, 9000, (4, 4, 4), torch.float32, 0),     # GQA, one query head per unit
+    (2, 4, 4, 3000, (2, 3, 3), torch.float16, 6),      # 8-bit codes (polar kernel), forced splits
+    (1, 8, 8, 777, (4, 4, 4), torch.float32, 3),       # two-pass 12-bit kernel, ragged last split
+    (2, 8, 8, 20000, (3, 3, 2), torch.float32, 0),     # one-byte kernel, planner's splits
+    (1, 16, 4, 5000, (3, 3, 2), torch.bfloat16, 4),    # tensor-core kernel, forced splits
 ]
 
 
