@@ -2,8 +2,9 @@
 
 Outputs are compared with the oracle's fp64 attention over the same codes
 (and with the reference's own outputs in the golden fixtures).  Tolerance:
-max abs error <= 1e-3 for every query dtype (the north_star allows 2e-2 for
-bf16 queries; the kernel computes in fp32 on the exactly upcast query).
+max abs error <= 1e-3 for every query dtype on the fp32 kernels (the stated
+bound for bf16 queries is 2e-2; those kernels compute in fp32 on the exactly
+upcast query), 2e-2 on the tensor-core kernel, whose operands are bf16/fp16.
 """
 
 import numpy as np

@@ -2,7 +2,7 @@
 
 Codes must equal the oracle's except at rounding ties proven by the fp64
 classifier (oracle/ties.py); decoded vectors must agree to 1e-5 (fp32
-output; the north_star bar is 1e-3) and bf16/fp16 outputs to their rounding.
+output; the stated bound for fp32 is 1e-3) and bf16/fp16 outputs to their rounding.
 """
 
 import numpy as np
