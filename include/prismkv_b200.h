@@ -47,7 +47,7 @@ extern "C" {
 enum {
     PKV_OK = 0,
     PKV_ERR_INVALID = 1,      /* null pointer, bad shape, bits out of range      */
-    PKV_ERR_UNSUPPORTED = 2,  /* well-formed but outside what this build runs    */
+    PKV_ERR_UNSUPPORTED = 2,  /* well-formed but outside what this library runs  */
     PKV_ERR_ALIGNMENT = 3,    /* pointer or stride misaligned for the call       */
     PKV_ERR_WORKSPACE = 4,    /* workspace missing or smaller than required      */
     PKV_ERR_CUDA = 5,         /* CUDA runtime reported an error (launch/config)  */

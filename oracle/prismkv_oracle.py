@@ -1,9 +1,9 @@
 """CPU oracle for the PrismKV quantized-KV hot path.
 
-TEST INFRASTRUCTURE ONLY.  This module is the checker the CUDA path is
+TEST INFRASTRUCTURE ONLY.  This module is the oracle the CUDA path is
 compared against.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
 ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it,
-and only as the checker or as the timed CPU reference -- never as part of
+and only to check results or as the timed CPU reference -- never as part of
 the product path in ``prismkv_b200``.
 
 It restates, in NumPy, the reference's CPU algorithm (PrismKV v1.4.1, whose
@@ -376,7 +376,7 @@ def polar_attention_forward_f32(q: np.ndarray, k_codes: np.ndarray, v: np.ndarra
     Follows the reference step by step (rotate q, unpack codes, uniform
     dequant, polar -> cartesian query, three contractions, scale, softmax,
     weights @ v).  This is the CPU path the benchmark times as the
-    reference; the checker uses :func:`attention`.  ``v`` is the decoded
+    reference; results are checked against :func:`attention`.  ``v`` is the decoded
     value tensor (B, H, Sk, d).  Returns (output, weights).
     """
     q = np.asarray(q, dtype=F32)

@@ -66,7 +66,7 @@ const char* pkv_strerror(int status) {
     switch (status) {
         case PKV_OK: return "ok";
         case PKV_ERR_INVALID: return "invalid argument (null pointer, shape, dtype or bit widths)";
-        case PKV_ERR_UNSUPPORTED: return "unsupported configuration for this build";
+        case PKV_ERR_UNSUPPORTED: return "unsupported configuration for this library";
         case PKV_ERR_ALIGNMENT: return "misaligned pointer or stride";
         case PKV_ERR_WORKSPACE: return "workspace missing or too small";
         case PKV_ERR_CUDA: return "CUDA runtime error";
