@@ -175,6 +175,14 @@ __device__ __forceinline__ BinGuess make_guess(const float* thr, int nz, int nr,
     return g;
 }
 
+// sqrt for a first guess only (hardware approximation, relative error ~2^-23; 0, +inf and NaN
+// map to themselves): the exact r^2 threshold count around the guess decides the bin
+__device__ __forceinline__ float guess_sqrt(float v) {
+    float r;
+    asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+
 __device__ __forceinline__ int guess_count(float v, float x0, float xi) {
     return __float2int_rd(fmaf(v - x0, xi, 1.f));  // saturating (no overflow at +-inf); NaN gives 0
 }
@@ -200,7 +208,7 @@ __device__ __forceinline__ uint32_t encode_triplet(const CodecArgs& a, const flo
         const int nt = (1 << a.bits_t) - 1;
         int ir, it;
         if (g) {
-            ir = count_ge_window(thr + nz, nr, s, guess_count(sqrtf(s), g->r0, g->ri));
+            ir = count_ge_window(thr + nz, nr, s, guess_count(guess_sqrt(s), g->r0, g->ri));
             it = count_ge_window(thr + nz + nr, nt, th, guess_count(th, g->t0, g->ti));
         } else {
             ir = count_ge(thr + nz, a.bits_r, s);
