@@ -125,12 +125,12 @@ __device__ __forceinline__ int nearest_centroid_cells(const CodecArgs& a, int iz
         const float fx = (x - a.cell_lo) * a.cell_scale, fy = (y - a.cell_lo) * a.cell_scale;
         if (fx >= 0.f && fy >= 0.f && fx < (float)a.cell_grid && fy < (float)a.cell_grid) {
             const int cell = (iz * a.cell_grid + (int)fy) * a.cell_grid + (int)fx;
+            // the count and the cell's candidate row (one 16-byte load) are fetched together
+            static_assert(kCellMax == 16, "one 16-byte row per cell");
             const int n = __ldg(a.cell_cnt + cell);
+            const uint4 row = __ldg(reinterpret_cast<const uint4*>(a.cell_idx) + cell);
             if (n <= kCellMax) {
-                // the cell's candidate list is one 16-byte row: a single load, then the scan in
-                // list (ascending index) order with a strict compare keeps the first minimum
-                static_assert(kCellMax == 16, "one 16-byte row per cell");
-                const uint4 row = __ldg(reinterpret_cast<const uint4*>(a.cell_idx) + cell);
+                // scan in list (ascending index) order; a strict compare keeps the first minimum
                 const uint32_t w4[4] = {row.x, row.y, row.z, row.w};
                 float best = INFINITY;
                 int bi = 0;
