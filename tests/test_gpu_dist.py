@@ -27,29 +27,37 @@ def _worker(rank, world, port, results):
     try:
         import oracle
         from prismkv_b200 import StackedPlaneQuantizer
-        from prismkv_b200.dist import batch_shard_decode, shard_range, split_sequence_decode
-        q = StackedPlaneQuantizer(96, 4, 4, 4, seed=42)
-        B, Hq, Hkv, S = 2, 16, 4, 3001
-        g = torch.Generator().manual_seed(9)
-        k = torch.randn(B * Hkv * S, 96, generator=g)
-        v = torch.randn(B * Hkv * S, 96, generator=g)
-        kc = q.encode_compact(k.to(dev)).view(B, Hkv, S, 32)
-        vc = q.encode_compact(v.to(dev)).view(B, Hkv, S, 32)
-        qv = torch.randn(B, Hq, 96, generator=g).to(dev)
-        a, b = shard_range(S, world, rank)
-        out = split_sequence_decode(q, qv, kc[:, :, a:b].contiguous(), vc[:, :, a:b].contiguous())
-        p = oracle.QuantParams.default(96)
-        ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64),
-                               vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
-        err_seq = float(np.abs(out.cpu().numpy() - ref).max())
-        from prismkv_b200.dist import PeerExchange
-        ex = PeerExchange(B * Hq, 96, dev)
-        for _ in range(3):                       # both buffer halves, then the first again
-            outp = split_sequence_decode(q, qv, kc[:, :, a:b].contiguous(), vc[:, :, a:b].contiguous(), exchange=ex)
-            err_seq = max(err_seq, float(np.abs(outp.cpu().numpy() - ref).max()))
-        ba, bb = shard_range(B, world, rank)
-        outb = batch_shard_decode(q, qv[ba:bb].contiguous(), kc[ba:bb].contiguous(), vc[ba:bb].contiguous())
-        err_batch = float(np.abs(outb.cpu().numpy() - ref[ba:bb]).max())
+        from prismkv_b200.dist import PeerExchange, batch_shard_decode, shard_range, split_sequence_decode
+        err_seq = err_batch = 0.0
+        exchanges = []                               # kept alive until every rank is done reading
+        # shards on the two-pass 12-bit kernel, the one-pass 12-bit kernel (shards past 4096
+        # tokens) and the one-byte kernel, all in partial mode for the sequence split
+        for bits, S in (((4, 4, 4), 3001), ((4, 4, 4), 9001), ((3, 3, 2), 5001)):
+            q = StackedPlaneQuantizer(96, *bits, seed=42)
+            B, Hq, Hkv = 2, 16, 4
+            g = torch.Generator().manual_seed(9)
+            k = torch.randn(B * Hkv * S, 96, generator=g)
+            v = torch.randn(B * Hkv * S, 96, generator=g)
+            kc = q.encode_compact(k.to(dev)).view(B, Hkv, S, 32)
+            vc = q.encode_compact(v.to(dev)).view(B, Hkv, S, 32)
+            qv = torch.randn(B, Hq, 96, generator=g).to(dev)
+            a, b = shard_range(S, world, rank)
+            out = split_sequence_decode(q, qv, kc[:, :, a:b].contiguous(), vc[:, :, a:b].contiguous())
+            p = oracle.QuantParams.default(96, *bits)
+            ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64),
+                                   vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
+            err_seq = max(err_seq, float(np.abs(out.cpu().numpy() - ref).max()))
+            ex = PeerExchange(B * Hq, 96, dev)
+            exchanges.append(ex)
+            for _ in range(3):                       # both buffer halves, then the first again
+                outp = split_sequence_decode(q, qv, kc[:, :, a:b].contiguous(), vc[:, :, a:b].contiguous(),
+                                             exchange=ex)
+                err_seq = max(err_seq, float(np.abs(outp.cpu().numpy() - ref).max()))
+            ba, bb = shard_range(B, world, rank)
+            outb = batch_shard_decode(q, qv[ba:bb].contiguous(), kc[ba:bb].contiguous(), vc[ba:bb].contiguous())
+            err_batch = max(err_batch, float(np.abs(outb.cpu().numpy() - ref[ba:bb]).max()))
+        torch.cuda.synchronize()
+        torch.distributed.barrier()                  # no rank frees a buffer a peer still reads
         torch.cuda.synchronize()
         results.put((rank, err_seq, err_batch))
     finally:
