@@ -129,3 +129,36 @@ def test_split_bf16x3_exact_and_sign_preserving():
         assert (np.sign(parts) == np.sign(R)[None]).all() and (parts != 0).all()
     z = split_bf16x3(np.array([[0.0, 1.0, -3.0]], np.float32))
     assert (z[:, 0, 0] == 0).all()                      # an exact zero stays zero
+
+
+def test_centroid_cells_contain_every_nearest_centroid():
+    """Every point of a grid cell has its nearest centroid (fp64) among the cell's candidates,
+    in ascending index order: the device scan over the candidates then equals the full scan.
+    Points at random, at cell edges and at the grid's rim."""
+    from prismkv_b200.synthetic import synthetic_codebook
+    from prismkv_b200.tables import CELL_GRID, CELL_MAX, centroid_cells
+    r_max = math.sqrt(96.0)
+    cb = synthetic_codebook(4, 256, r_max, 11).numpy()
+    idx, cnt = centroid_cells(cb, r_max)
+    assert idx.shape == (4, CELL_GRID, CELL_GRID, CELL_MAX) and cnt.shape == (4, CELL_GRID, CELL_GRID)
+    w = 2 * r_max / CELL_GRID
+    rng = np.random.default_rng(3)
+    pts = [rng.standard_normal((20000, 2)) * s for s in (0.5, 1.5, 4.0)]
+    edges = (rng.integers(0, CELL_GRID + 1, (20000, 2)) * w - r_max)          # on cell edges
+    rim = np.stack([np.full(2000, -r_max), rng.uniform(-r_max, r_max, 2000)], 1)
+    P = np.concatenate(pts + [edges, rim]).astype(np.float32)
+    P = P[(np.abs(P) < r_max).all(1)]                                       # inside the grid
+    iz = rng.integers(0, 4, len(P))
+    fx = np.floor((P[:, 0] + np.float32(r_max)) * np.float32(CELL_GRID / (2 * r_max))).astype(int)
+    fy = np.floor((P[:, 1] + np.float32(r_max)) * np.float32(CELL_GRID / (2 * r_max))).astype(int)
+    fx, fy = np.clip(fx, 0, CELL_GRID - 1), np.clip(fy, 0, CELL_GRID - 1)
+    d = ((P[:, None, :].astype(np.float64) - cb[iz].astype(np.float64)) ** 2).sum(-1)
+    nearest = d.argmin(1)
+    n = cnt[iz, fy, fx]
+    assert (n != 255).mean() > 0.999 and n[n != 255].mean() < 4
+    ok = n != 255
+    cand = idx[iz, fy, fx].astype(int)[ok]                                  # (points, CELL_MAX)
+    valid = np.arange(CELL_MAX)[None, :] < n[ok][:, None]
+    assert (((np.diff(cand, axis=1) > 0) | ~valid[:, 1:]).all())             # ascending indices
+    hit = ((cand == nearest[ok][:, None]) & valid).any(1)
+    assert hit.all(), P[ok][~hit][:5]
