@@ -10,8 +10,9 @@
 // shared memory for the CTA's lifetime).
 //
 //  * K: score table T[c][j] = q'_j . (z, x, y)(c) over all 256 byte values c and the 32
-//    triplets j (32 KB), z and (x, y) straight from the codec's decode tables.  Lane l reads word l%8 of token 4s + l/8 (four codes) and takes the word's
-//    bytes starting at byte l/8, so the 32 table loads of a step hit 32 distinct banks.
+//    triplets j (32 KB), z and (x, y) straight from the codec's decode tables.  Lane l
+//    reads word l%8 of token 4s + l/8 (four codes) and takes the word's bytes starting at
+//    byte l/8, so the 32 table loads of a step hit 32 distinct banks.
 //    An 8-lane transpose-reduce completes 32 scores per 8 steps.
 //  * V: lane l reads 8 codes (triplets 8(l%4)..+7) of token l/4 of a group of 8 tokens.
 //    Each byte is moved to bits 8..15 of a word.  z comes from its bits under the 2^23
