@@ -24,3 +24,26 @@ def test_reference_arm_prints_one_contract_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_partition_shards_the_sharded_workloads_and_replicates_the_rest():
+    """longctx splits its sequence and aggressive-332 its batch across ranks, covering every
+    token / row exactly once; the other workloads run one replica per rank."""
+    sys.path.insert(0, ROOT)
+    import bench
+    from prismkv_b200.synthetic import WORKLOADS
+    for ws in (1, 2, 3, 8):
+        for name, w in WORKLOADS.items():
+            parts = [bench._partition(w, ws, r) for r in range(ws)]
+            modes = {m for m, _, _ in parts}
+            if ws > 1 and name == "longctx-splitseq":
+                assert modes == {"sequence"}
+                spans = [s for _, _, s in parts]
+                assert spans[0][0] == 0 and spans[-1][1] == w.seq_len
+                assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+                assert sum(lw.seq_len for _, lw, _ in parts) == w.seq_len
+            elif ws > 1 and name == "aggressive-332":
+                assert modes == {"batch"}
+                assert sum(lw.batch for _, lw, _ in parts) == w.batch
+            else:
+                assert modes == {"replicas"} and all(lw == w for _, lw, _ in parts)
