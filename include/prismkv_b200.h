@@ -3,7 +3,8 @@
  *
  * Every entry point takes plain device pointers, element counts, strides and
  * a CUDA stream (passed as `void *`, it is a `cudaStream_t`), returns an int
- * status (0 = PKV_OK) and never allocates device memory.  Buffers are owned
+ * status (0 = PKV_OK) and allocates no device memory (pkv_xr_alloc, the
+ * one-time set-up of the split-sequence exchange, is the exception).  Buffers are owned
  * by the caller.  Kernels are enqueued on the given stream; no entry point
  * synchronises the host.  Entry points are re-entrant: concurrent calls on
  * different streams are safe as long as they do not share a workspace.
@@ -24,6 +25,8 @@
  *                      kernel src/prismkv/cuda/polar_attn_kernel.cu:142-336,
  *                      Python contract src/prismkv/cuda/__init__.py:23-61
  *   pkv_lse_combine    (new) log-sum-exp merge of split-sequence partials
+ *   pkv_attn_decode_xr (new) split-sequence decode with the cross-GPU merge
+ *                      inside the attention kernel (pkv_xr_* set it up)
  */
 #ifndef PRISMKV_B200_H
 #define PRISMKV_B200_H
@@ -185,7 +188,7 @@ PKV_API int pkv_attn_decode(const pkv_codec *c, const pkv_attn_args *a,
  * (introspection for tests and benchmarks; launches nothing; the output
  * pointers of `a` may be null).                                           */
 enum { PKV_KERNEL_MHA12 = 1, PKV_KERNEL_POLAR = 2, PKV_KERNEL_LUT = 3, PKV_KERNEL_TC = 4, PKV_KERNEL_MHA8 = 5,
-       PKV_KERNEL_MHA12_STREAM = 6 };
+       PKV_KERNEL_MHA12_STREAM = 6, PKV_KERNEL_GQA12 = 7 };
 typedef struct pkv_attn_plan {
     int32_t kernel;            /* PKV_KERNEL_*                                  */
     int32_t num_splits;        /* sequence splits per (batch, kv head)          */
@@ -234,6 +237,57 @@ PKV_API int pkv_lse_combine(const pkv_codec *c, const float *partials, int32_t n
 PKV_API int pkv_lse_combine_gather(const pkv_codec *c, const float *const *part_ptrs, int32_t n_parts,
                            int64_t part_offset, int32_t rows, float *out, int64_t out_row_stride,
                            void *stream);
+
+/* ---- split-sequence decode across GPUs (one process per GPU) ------------ *
+ * Each rank holds a contiguous token shard of every (batch, KV head) and runs
+ * pkv_attn_decode_xr over it.  The exchange happens inside that one kernel:
+ * when a unit's (batch row, its query heads) partial softmax state
+ * [m (log2 units), l, o_rot[dim]] is final on a rank, the rank stores it into
+ * slot `rank` of EVERY rank's exchange buffer (plain peer stores over NVLink),
+ * fences, and adds one to the unit's arrival counter at its owner rank
+ * (unit % world).  The rank whose addition completes the count merges the
+ * world partials (log-sum-exp), applies R once and stores the output rows into
+ * every rank's buffer, then counts the unit done at every rank.  The last CTA
+ * of each rank's kernel waits -- bounded by wait_limit_us, measured with the
+ * device clock -- until all units are done there, then resets its counters.
+ * On expiry it sets the device error word to 4 (read by pkv_device_error) and
+ * returns; the counters are then left as they were, and every rank must call
+ * pkv_xr_reset (after a host-side agreement that the step failed) before the
+ * next step.  No
+ * multicast object is involved: buffers come from cudaMalloc and are mapped
+ * into the peers with CUDA IPC.  Replaces the reference's nothing: the
+ * reference decodes on one CPU (polar_attention.py:277-309); sharding the
+ * sequence is the decomposition of that same softmax.
+ *
+ * Buffer layout (pkv_xr_layout): partial slots [world][rows][dim + 2] f32,
+ * output rows [rows][dim] f32 (rows = batch * q_heads, row b * q_heads + h),
+ * unit counters, a done counter and a CTA counter; zero when allocated.      */
+#define PKV_XR_MAX_RANKS 8
+typedef struct pkv_exchange {
+    int32_t world, rank;
+    void *buffers[PKV_XR_MAX_RANKS];   /* every rank's buffer, mapped in this process */
+    uint32_t wait_limit_us;            /* bound on the completion wait              */
+} pkv_exchange;
+typedef struct pkv_xr_layout {
+    uint64_t bytes;                    /* buffer size                               */
+    uint64_t out_offset;               /* byte offset of the output rows            */
+    int32_t rows, units;
+} pkv_xr_layout;
+PKV_API int pkv_xr_layout_for(const pkv_codec *c, const pkv_attn_args *a, int32_t world, pkv_xr_layout *out);
+/* Set-up (not the decode path): allocate a zeroed exchange buffer and export
+ * its CUDA IPC handle (64 bytes); open / close a peer's buffer from its
+ * handle; free this rank's buffer (after every peer has closed it).          */
+PKV_API int pkv_xr_alloc(uint64_t bytes, void **dev_ptr, void *ipc_handle_out);
+PKV_API int pkv_xr_open(const void *ipc_handle, void **dev_ptr);
+PKV_API int pkv_xr_close(void *peer_ptr);
+PKV_API int pkv_xr_free(void *dev_ptr);
+/* Zero this rank's counters (after an expired wait; every rank, between steps). */
+PKV_API int pkv_xr_reset(const pkv_codec *c, const pkv_attn_args *a, const pkv_exchange *x, void *stream);
+/* a->partial_only must be 0 and a->out is unused: outputs land in every rank's
+ * buffer at out_offset.  a->seq_len is this rank's shard length; batch, heads
+ * and the plan's unit decomposition must agree across ranks.                  */
+PKV_API int pkv_attn_decode_xr(const pkv_codec *c, const pkv_attn_args *a, void *workspace, size_t workspace_bytes,
+                               const pkv_exchange *x, void *stream);
 
 /* Scores of prismkv_cuda.polar_attn_fwd: out[b,h,i,j] =
  * scale * <q_rot[b,h,i], dequant(k_codes[b,h,j])> with the uniform polar

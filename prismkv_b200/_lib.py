@@ -24,7 +24,10 @@ DTYPE_CODES = {torch.float32: PKV_F32, torch.bfloat16: PKV_BF16, torch.float16: 
 EXPORTED = ("pkv_abi_version", "pkv_strerror", "pkv_device_error", "pkv_encode", "pkv_decode",
             "pkv_attn_workspace_size", "pkv_workspace_init", "pkv_attn_decode", "pkv_lse_combine",
             "pkv_polar_scores", "pkv_attn_decode_noalloc", "pkv_attn_describe", "pkv_encode_append",
-            "pkv_decode_cache", "pkv_lse_combine_gather")
+            "pkv_decode_cache", "pkv_lse_combine_gather", "pkv_xr_layout_for", "pkv_xr_alloc", "pkv_xr_open",
+            "pkv_xr_close", "pkv_xr_free", "pkv_xr_reset", "pkv_attn_decode_xr")
+XR_MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
 
 
 class PkvCodec(ctypes.Structure):
@@ -53,8 +56,16 @@ class PkvAttnPlan(ctypes.Structure):
                 ("threads", c_int32), ("smem_bytes", c_int32), ("ctas_per_sm", c_int32), ("balanced", c_int32)]
 
 
+class PkvExchange(ctypes.Structure):
+    _fields_ = [("world", c_int32), ("rank", c_int32), ("buffers", c_void_p * 8), ("wait_limit_us", ctypes.c_uint32)]
+
+
+class PkvXrLayout(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_uint64), ("out_offset", ctypes.c_uint64), ("rows", c_int32), ("units", c_int32)]
+
+
 KERNEL_NAMES = {1: "attn_mha12_kernel", 2: "attn_polar_kernel", 3: "attn_lut_kernel", 4: "attn_tc_kernel",
-                5: "attn_mha8_kernel", 6: "attn_mha12_stream_kernel"}
+                5: "attn_mha8_kernel", 6: "attn_mha12_stream_kernel", 7: "attn_gqa12_kernel"}
 
 _lock = threading.Lock()
 _lib = None
@@ -93,6 +104,20 @@ def _declare(lib):
     lib.pkv_lse_combine_gather.restype = c_int32
     lib.pkv_lse_combine_gather.argtypes = [P(PkvCodec), c_void_p, c_int32, c_int64, c_int32, c_void_p, c_int64,
                                            c_void_p]
+    lib.pkv_xr_layout_for.restype = c_int32
+    lib.pkv_xr_layout_for.argtypes = [P(PkvCodec), P(PkvAttnArgs), c_int32, P(PkvXrLayout)]
+    lib.pkv_xr_alloc.restype = c_int32
+    lib.pkv_xr_alloc.argtypes = [ctypes.c_uint64, P(c_void_p), c_void_p]
+    lib.pkv_xr_open.restype = c_int32
+    lib.pkv_xr_open.argtypes = [c_void_p, P(c_void_p)]
+    lib.pkv_xr_close.restype = c_int32
+    lib.pkv_xr_close.argtypes = [c_void_p]
+    lib.pkv_xr_free.restype = c_int32
+    lib.pkv_xr_free.argtypes = [c_void_p]
+    lib.pkv_xr_reset.restype = c_int32
+    lib.pkv_xr_reset.argtypes = [P(PkvCodec), P(PkvAttnArgs), P(PkvExchange), c_void_p]
+    lib.pkv_attn_decode_xr.restype = c_int32
+    lib.pkv_attn_decode_xr.argtypes = [P(PkvCodec), P(PkvAttnArgs), c_void_p, c_size_t, P(PkvExchange), c_void_p]
     lib.pkv_polar_scores.restype = c_int32
     lib.pkv_polar_scores.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32,
                                      P(c_float), P(c_int32), c_void_p, c_void_p]

@@ -243,13 +243,15 @@ class DeviceCodec:
                   scale: Optional[float] = None, seq_lens: Optional[torch.Tensor] = None,
                   out: Optional[torch.Tensor] = None, num_splits: int = 0,
                   partial: bool = False, workspace: Optional[torch.Tensor] = None,
-                  partial_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                  partial_out: Optional[torch.Tensor] = None, exchange=None) -> torch.Tensor:
         """Decode attention over packed codes.
 
         q (B, Hq, dim) [or (B, Hq, 1, dim)], k/v codes (B, Hkv, S, m) with unit
         token/triplet strides.  Returns (B, Hq, dim) fp32, or with
         ``partial=True`` the (B, Hq, dim + 2) rotated-space partials
-        [m_max, l, o] for a cross-shard merge.
+        [m_max, l, o] for a cross-shard merge.  With ``exchange`` (a
+        ``dist.SequenceExchange``) the codes are this rank's token shard and the
+        merged rows of all ranks land in ``exchange.out`` (pkv_attn_decode_xr).
         """
         for t, n in ((q, "q"), (k_codes, "k_codes"), (v_codes, "v_codes")):
             _lib.require_cuda(t, n)
@@ -276,6 +278,8 @@ class DeviceCodec:
             scale = self.dim ** -0.5
         if seq_lens is not None:
             seq_lens = seq_lens.to(device=self.device, dtype=torch.int32).contiguous()
+        if exchange is not None:
+            partial, out, partial_out = False, None, None
         if partial:
             if partial_out is None:
                 partial_out = torch.empty((B, Hq, self.dim + 2), dtype=torch.float32, device=self.device)
@@ -284,13 +288,23 @@ class DeviceCodec:
                 raise ValueError("partial_out must be a contiguous float32 tensor of B * Hq * (dim + 2)")
         else:
             partial_out = None
-            if out is None:
+            if out is None and exchange is None:
                 out = torch.empty((B, Hq, self.dim), dtype=torch.float32, device=self.device)
         a = self._attn_args(q, k_codes, v_codes, scale, seq_lens, out, num_splits, partial_out)
         lib = _lib.load()
         with torch.cuda.device(self.device):
-            need = lib.pkv_attn_workspace_size(ctypes.byref(self.struct), ctypes.byref(a))
+            a_ws = a
+            if exchange is not None:            # the workspace size needs an output to plan with
+                a_ws = self._attn_args(q, k_codes, v_codes, scale, seq_lens, exchange.out, num_splits, None)
+            need = lib.pkv_attn_workspace_size(ctypes.byref(self.struct), ctypes.byref(a_ws))
             ws = workspace if workspace is not None else (self.workspace(need) if need else None)
+            if exchange is not None:
+                rc = lib.pkv_attn_decode_xr(ctypes.byref(self.struct), ctypes.byref(a),
+                                            ws.data_ptr() if ws is not None else None,
+                                            ws.numel() if ws is not None else 0, ctypes.byref(exchange.struct),
+                                            self._stream())
+                _lib.check(rc, "pkv_attn_decode_xr")
+                return exchange.out
             rc = lib.pkv_attn_decode(ctypes.byref(self.struct), ctypes.byref(a),
                                      ws.data_ptr() if ws is not None else None,
                                      ws.numel() if ws is not None else 0, self._stream())

@@ -5,6 +5,7 @@
 // reference's TORCH_CHECKs raise (polar_attn_kernel.cu:274-309).
 
 #include <cmath>
+#include <cstring>
 
 #include "pkv_common.cuh"
 
@@ -16,7 +17,10 @@ int launch_decode(const pkv_codec* c, const void* codes, int cb, int64_t n, int6
 size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a);
 void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out);
 bool attn_group_supported(const pkv_codec* c, const pkv_attn_args* a);
-int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st);
+int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st,
+                const pkv_exchange* xr = nullptr);
+void xr_layout(const pkv_codec* c, const pkv_attn_args* a, int world, pkv_xr_layout* out);
+void xr_counter_span(const pkv_codec* c, const pkv_attn_args* a, int world, size_t* off, size_t* len);
 int launch_lse_combine(const pkv_codec* c, const float* parts, int n_parts, int64_t part_stride, int rows,
                        float* out, int64_t out_rs, cudaStream_t st);
 int launch_lse_combine_gather(const pkv_codec* c, const float* const* part_ptrs, int n_parts, int64_t part_offset,
@@ -200,6 +204,78 @@ int pkv_attn_decode(const pkv_codec* c, const pkv_attn_args* a, void* workspace,
     if (rc) return rc;
     if (a->batch == 0) return PKV_OK;
     return pkv::launch_attn(c, a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+// ---- split-sequence exchange ----------------------------------------------
+static int check_xr(const pkv_exchange* x) {
+    if (!x || x->world < 1 || x->world > PKV_XR_MAX_RANKS || x->rank < 0 || x->rank >= x->world) return PKV_ERR_INVALID;
+    for (int s = 0; s < x->world; ++s)
+        if (!x->buffers[s] || reinterpret_cast<uintptr_t>(x->buffers[s]) % 256 != 0) return PKV_ERR_INVALID;
+    return PKV_OK;
+}
+
+int pkv_xr_layout_for(const pkv_codec* c, const pkv_attn_args* a, int32_t world, pkv_xr_layout* out) {
+    if (!out || world < 1 || world > PKV_XR_MAX_RANKS) return PKV_ERR_INVALID;
+    const int rc = check_attn(c, a, false);
+    if (rc) return rc;
+    if (!pkv::attn_group_supported(c, a)) return PKV_ERR_UNSUPPORTED;
+    pkv::xr_layout(c, a, world, out);
+    return PKV_OK;
+}
+
+int pkv_xr_alloc(uint64_t bytes, void** dev_ptr, void* ipc_handle_out) {
+    if (!dev_ptr || !ipc_handle_out || bytes == 0) return PKV_ERR_INVALID;
+    void* ptr = nullptr;
+    if (cudaMalloc(&ptr, bytes) != cudaSuccess) return PKV_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(ptr, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) {
+        cudaFree(ptr);
+        return PKV_ERR_CUDA;
+    }
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    memcpy(ipc_handle_out, &h, sizeof(h));
+    *dev_ptr = ptr;
+    return PKV_OK;
+}
+
+int pkv_xr_open(const void* ipc_handle, void** dev_ptr) {
+    if (!ipc_handle || !dev_ptr) return PKV_ERR_INVALID;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    return cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? PKV_OK : PKV_ERR_CUDA;
+}
+
+int pkv_xr_close(void* peer_ptr) {
+    if (!peer_ptr) return PKV_ERR_INVALID;
+    return cudaIpcCloseMemHandle(peer_ptr) == cudaSuccess ? PKV_OK : PKV_ERR_CUDA;
+}
+
+int pkv_xr_free(void* dev_ptr) {
+    if (!dev_ptr) return PKV_ERR_INVALID;
+    return cudaFree(dev_ptr) == cudaSuccess ? PKV_OK : PKV_ERR_CUDA;
+}
+
+int pkv_xr_reset(const pkv_codec* c, const pkv_attn_args* a, const pkv_exchange* x, void* stream) {
+    int rc = check_xr(x);
+    if (rc) return rc;
+    rc = check_attn(c, a, false);
+    if (rc) return rc;
+    size_t off = 0, len = 0;
+    pkv::xr_counter_span(c, a, x->world, &off, &len);
+    return cudaMemsetAsync(static_cast<uint8_t*>(x->buffers[x->rank]) + off, 0, len,
+                           static_cast<cudaStream_t>(stream)) == cudaSuccess ? PKV_OK : PKV_ERR_CUDA;
+}
+
+int pkv_attn_decode_xr(const pkv_codec* c, const pkv_attn_args* a, void* workspace, size_t workspace_bytes,
+                       const pkv_exchange* x, void* stream) {
+    int rc = check_xr(x);
+    if (rc) return rc;
+    if (a && a->partial_only) return PKV_ERR_INVALID;
+    rc = check_attn(c, a, false);
+    if (rc) return rc;
+    if (a->batch == 0) return PKV_OK;
+    if (!pkv::attn_group_supported(c, a)) return PKV_ERR_UNSUPPORTED;
+    return pkv::launch_attn(c, a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), x);
 }
 
 int pkv_lse_combine(const pkv_codec* c, const float* partials, int32_t n_parts, int64_t part_stride, int32_t rows,

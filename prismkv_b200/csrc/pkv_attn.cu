@@ -74,6 +74,13 @@ struct AttnParams {
     // Hu: work units per batch row -- Hkv, or Hq when every query head is its own unit reading
     // KV head hq / Gq (grouped heads through a one-head kernel; the group's re-reads hit L2)
     int Hu, Gq;
+    // split-sequence exchange (pkv_attn_decode_xr) when xr_world > 0: every rank's exchange buffer
+    // (partial slots, output rows, counters at the byte offsets below), this rank's index, the
+    // units every rank counts, and the bound on the completion wait
+    int xr_world, xr_rank, xr_units;
+    uint8_t* xr_buf[PKV_XR_MAX_RANKS];
+    int64_t xr_out_off, xr_cnt_off, xr_done_off;
+    uint64_t xr_wait_ns;
 };
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -224,16 +231,180 @@ __device__ __forceinline__ void rotate_query(const AttnParams& p, const ItemRang
     }
 }
 
-// Per-item epilogue shared by both kernels.  Inputs in shared memory, per head
-// g < greal: sM[g] (running max, log2 units), sL[g], sO[g*dim + k] (unnormalised
-// rotated-space output).  Writes the partial row, or merges splits and writes
-// out = (o / l) @ R.  All `nthr` consumer threads call it; barrier id 1.
+// ---------------------------------------------------------------------------
+// split-sequence exchange primitives (system scope: the peers are other GPUs)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t* ptr, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.sys.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void red_add_release_sys(uint32_t* ptr, uint32_t v) {
+    asm volatile("red.add.release.sys.global.u32 [%0], %1;" :: "l"(ptr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Output element (query head g of the item's unit, dim i): the caller's output, or in exchange
+// mode the output rows of every rank's buffer.
+__device__ __forceinline__ void store_out(const AttnParams& p, const ItemRange& r, int g, int i, float v) {
+    const int hq = r.hk * p.G + g;
+    if (p.xr_world > 0) {
+        const int64_t off = p.xr_out_off + (((int64_t)r.b * p.Hq + hq) * p.dim + i) * 4;
+        for (int s = 0; s < p.xr_world; ++s) *reinterpret_cast<float*>(p.xr_buf[s] + off) = v;
+    } else {
+        p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
+    }
+}
+
+// Exchange mode: element k of this rank's final partial row of query head g ([m (log2 units), l,
+// o_rot]) into slot xr_rank of every rank's buffer.
+__device__ __forceinline__ void xr_publish(const AttnParams& p, const ItemRange& r, int g, int k, float val) {
+    const int64_t row = (int64_t)r.b * p.Hq + r.hk * p.G + g;
+    const int64_t off = (((int64_t)p.xr_rank * p.B * p.Hq + row) * (p.dim + 2) + k) * 4;
+    for (int s = 0; s < p.xr_world; ++s) *reinterpret_cast<float*>(p.xr_buf[s] + off) = val;
+}
+
+// out rows of the item's unit = (sFin rows) @ R, through store_out.  With parts > 1, up to
+// max_parts threads share an output, each summing a slice of k with two chains; sO (at least
+// max_parts * G * dim floats, dead by now) holds their partial sums.  With one part, each thread
+// batches 16 loads of R ahead of its FMAs.
+__device__ void rotate_out(const AttnParams& p, const ItemRange& r, float* sO, const float* sFin, const float* Rp,
+                           int pitch, int tid, int nthr, int max_parts) {
+    const int dim = p.dim, greal = p.G;
+    named_bar_sync(1, nthr);
+    const int gd = greal * dim;
+    const int parts = max(1, min(max_parts, nthr / gd));
+    if (parts == 1) {
+        for (int idx = tid; idx < gd; idx += nthr) {
+            const int g = idx / dim, i = idx % dim;
+            float v = 0.f;
+            for (int k0 = 0; k0 < dim; k0 += 16) {
+                float rv[16];
+                #pragma unroll
+                for (int u = 0; u < 16; ++u) rv[u] = (k0 + u < dim) ? Rp[(k0 + u) * pitch + i] : 0.f;
+                #pragma unroll
+                for (int u = 0; u < 16; ++u)
+                    if (k0 + u < dim) v = fmaf(sFin[g * dim + k0 + u], rv[u], v);
+            }
+            store_out(p, r, g, i, v);
+        }
+        return;
+    }
+    const int klen = (dim + parts - 1) / parts;
+    for (int idx = tid; idx < gd * parts; idx += nthr) {
+        const int part = idx / gd, gi = idx % gd, g = gi / dim, i = gi % dim;
+        const int k1 = min(dim, (part + 1) * klen);
+        const float* f = sFin + g * dim;
+        float v0 = 0.f, v1 = 0.f;
+        int k = part * klen;
+        #pragma unroll 8
+        for (; k + 1 < k1; k += 2) {
+            v0 = fmaf(f[k], Rp[k * pitch + i], v0);
+            v1 = fmaf(f[k + 1], Rp[(k + 1) * pitch + i], v1);
+        }
+        if (k < k1) v0 = fmaf(f[k], Rp[k * pitch + i], v0);
+        sO[idx] = v0 + v1;
+    }
+    named_bar_sync(1, nthr);
+    for (int gi = tid; gi < gd; gi += nthr) {
+        float v = 0.f;
+        for (int part = 0; part < parts; ++part) v += sO[part * gd + gi];
+        store_out(p, r, gi / dim, gi % dim, v);
+    }
+}
+
+// Exchange mode, after this rank's partial rows of the unit are in every rank's buffer: count
+// the arrival at the unit's owner rank; the rank that completes the count merges the world
+// partials from its own buffer (every rank stored into every buffer before counting), applies R
+// once, stores the rows into every rank's output and counts the unit done at every rank.
+__device__ void xr_arrive(const AttnParams& p, const ItemRange& r, float* sO, float* sFin, int* sflag,
+                          const float* Rp, int pitch, int tid, int nthr, int max_parts) {
+    const int dim = p.dim, greal = p.G;
+    __threadfence_system();
+    named_bar_sync(1, nthr);
+    if (tid == 0) {
+        const int unit = r.b * p.Hu + r.hk;
+        uint32_t* cnt = reinterpret_cast<uint32_t*>(p.xr_buf[unit % p.xr_world] + p.xr_cnt_off) + unit;
+        const uint32_t old = atom_add_acq_rel_sys(cnt, 1u);
+        const int last = (old == (uint32_t)p.xr_world - 1);
+        if (last) *reinterpret_cast<volatile uint32_t*>(cnt) = 0u;     // the next step counts from zero
+        sflag[0] = last;
+    }
+    named_bar_sync(1, nthr);
+    if (!sflag[0]) return;
+    const float* part = reinterpret_cast<const float*>(p.xr_buf[p.xr_rank]);
+    const int64_t slot = (int64_t)p.B * p.Hq * (dim + 2);
+    for (int idx = tid; idx < greal * dim; idx += nthr) {
+        const int g = idx / dim, k = idx % dim;
+        const float* src = part + ((int64_t)r.b * p.Hq + r.hk * greal + g) * (dim + 2);
+        float M = -INFINITY;
+        for (int s = 0; s < p.xr_world; ++s) M = fmaxf(M, __ldcg(src + s * slot));
+        float v = 0.f, l = 0.f;
+        for (int s = 0; s < p.xr_world; ++s) {
+            const float ms = __ldcg(src + s * slot);
+            const float f = (ms == -INFINITY) ? 0.f : fast_exp2(ms - M);
+            l = fmaf(__ldcg(src + s * slot + 1), f, l);
+            v = fmaf(__ldcg(src + s * slot + 2 + k), f, v);
+        }
+        sFin[g * dim + k] = (l > 0.f) ? v / l : 0.f;
+    }
+    rotate_out(p, r, sO, sFin, Rp, pitch, tid, nthr, max_parts);
+    __threadfence_system();
+    named_bar_sync(1, nthr);
+    if (tid == 0)
+        for (int s = 0; s < p.xr_world; ++s)
+            red_add_release_sys(reinterpret_cast<uint32_t*>(p.xr_buf[s] + p.xr_done_off), 1u);
+}
+
+// Exchange mode, once per CTA after its last item: the rank's last CTA waits until every unit's
+// output rows have arrived in this rank's buffer, bounded by xr_wait_ns of device time; on expiry
+// it sets the device error word and leaves the counters as they are (the host resets them).
+__device__ void xr_kernel_tail(const AttnParams& p, int tid, int nthr) {
+    if (p.xr_world <= 0) return;
+    named_bar_sync(1, nthr);
+    if (tid != 0) return;
+    uint32_t* done = reinterpret_cast<uint32_t*>(p.xr_buf[p.xr_rank] + p.xr_done_off);
+    uint32_t* ctas = done + 1;
+    __threadfence();
+    if (atomicAdd(ctas, 1u) != gridDim.x - 1) return;
+    const uint64_t t0 = global_ns();
+    while (ld_acquire_sys(done) < (uint32_t)p.xr_units) {
+        if (global_ns() - t0 > p.xr_wait_ns) {
+            flag_error(kErrPeerWait);
+            return;
+        }
+        __nanosleep(200);
+    }
+    *reinterpret_cast<volatile uint32_t*>(done) = 0u;
+    *reinterpret_cast<volatile uint32_t*>(ctas) = 0u;
+    __threadfence();
+}
+
+// Per-item epilogue shared by the kernels.  Inputs in shared memory, per head g < greal: sM[g]
+// (running max, log2 units), sL[g], sO[g*dim + k] (unnormalised rotated-space output).  Writes
+// the partial row, or merges splits and writes out = (o / l) @ R, or (exchange mode) publishes
+// the unit's partial rows to every rank and takes part in the cross-rank merge.  All `nthr`
+// consumer threads call it; barrier id 1.
 __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float* sM, const float* sL,
                             float* sO, float* sFin, int* sflag, const float* Rp, int pitch, int tid,
                             int nthr, int max_parts) {
     const int dim = p.dim, greal = p.G;
     const bool single = (r.nseg == 1);
-    bool finalize = single && !p.partial_only;
+    const bool xr = p.xr_world > 0;
+    bool finalize = single && !p.partial_only && !xr;
+    bool arrive = single && xr;
     for (int idx = tid; idx < greal * (dim + 2); idx += nthr) {
         const int g = idx / (dim + 2), k = idx % (dim + 2);
         const float M = sM[g], L = sL[g];
@@ -242,12 +413,14 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
             if (k >= 2) sFin[g * dim + (k - 2)] = (L > 0.f) ? sO[g * dim + (k - 2)] / L : 0.f;
         } else {
             const float val = (k == 0) ? M : (k == 1 ? L : sO[g * dim + (k - 2)]);
-            if (single) {
-                float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
-                dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : val;
-            } else {
+            if (!single) {
                 float* dst = p.ws_part + (((int64_t)r.b * p.Hq + hq) * p.slots + r.split) * (dim + 2);
                 dst[k] = val;
+            } else if (xr) {
+                xr_publish(p, r, g, k, val);
+            } else {
+                float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
+                dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : val;
             }
         }
     }
@@ -276,7 +449,9 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
                     lsw = fmaf(__ldcg(src + sp * (dim + 2) + 1), f, lsw);
                     if (k >= 2) v = fmaf(__ldcg(src + sp * (dim + 2) + k), f, v);
                 }
-                if (p.partial_only) {
+                if (xr) {
+                    xr_publish(p, r, g, k, (k == 0) ? M : (k == 1 ? lsw : v));
+                } else if (p.partial_only) {
                     float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
                     dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : (k == 1 ? lsw : v);
                 } else if (k >= 2) {
@@ -290,58 +465,14 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
                 float* rows = p.ws_part + ((int64_t)r.b * p.Hq + (int64_t)r.hk * greal + g) * p.slots * (dim + 2);
                 for (int k = tid; k < r.nseg * (dim + 2); k += nthr) rows[k] = 0.f;
             }
-            finalize = !p.partial_only;
+            finalize = !p.partial_only && !xr;
+            arrive = xr;
         }
     }
-    if (finalize) {
-        // out = fin @ R.  With parts > 1, up to max_parts threads share an output, each summing a
-        // slice of k with two chains; sO (at least max_parts * G * dim floats, dead by now) holds
-        // their partial sums.  With one part, each thread batches 16 loads of R ahead of its FMAs.
-        named_bar_sync(1, nthr);
-        const int gd = greal * dim;
-        const int parts = max(1, min(max_parts, nthr / gd));
-        if (parts == 1) {
-            for (int idx = tid; idx < gd; idx += nthr) {
-                const int g = idx / dim, i = idx % dim;
-                float v = 0.f;
-                for (int k0 = 0; k0 < dim; k0 += 16) {
-                    float rv[16];
-                    #pragma unroll
-                    for (int u = 0; u < 16; ++u) rv[u] = (k0 + u < dim) ? Rp[(k0 + u) * pitch + i] : 0.f;
-                    #pragma unroll
-                    for (int u = 0; u < 16; ++u)
-                        if (k0 + u < dim) v = fmaf(sFin[g * dim + k0 + u], rv[u], v);
-                }
-                const int hq = r.hk * greal + g;
-                p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
-            }
-        }
-        const int klen = (dim + parts - 1) / parts;
-        for (int idx = tid; parts > 1 && idx < gd * parts; idx += nthr) {
-            const int part = idx / gd, gi = idx % gd, g = gi / dim, i = gi % dim;
-            const int k1 = min(dim, (part + 1) * klen);
-            const float* f = sFin + g * dim;
-            float v0 = 0.f, v1 = 0.f;
-            int k = part * klen;
-            #pragma unroll 8
-            for (; k + 1 < k1; k += 2) {
-                v0 = fmaf(f[k], Rp[k * pitch + i], v0);
-                v1 = fmaf(f[k + 1], Rp[(k + 1) * pitch + i], v1);
-            }
-            if (k < k1) v0 = fmaf(f[k], Rp[k * pitch + i], v0);
-            sO[idx] = v0 + v1;
-        }
-        if (parts > 1) {
-            named_bar_sync(1, nthr);
-            for (int gi = tid; gi < gd; gi += nthr) {
-                float v = 0.f;
-                for (int part = 0; part < parts; ++part) v += sO[part * gd + gi];
-                const int g = gi / dim, i = gi % dim, hq = r.hk * greal + g;
-                p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
-            }
-        }
-    }
-    named_bar_sync(1, nthr);     // shared scratch is reused by the next item
+    if (arrive) xr_arrive(p, r, sO, sFin, sflag, Rp, pitch, tid, nthr, max_parts);
+    if (finalize) rotate_out(p, r, sO, sFin, Rp, pitch, tid, nthr, max_parts);
+    // the next item may overwrite sFin / sO / sflag only after every thread is done with them
+    named_bar_sync(1, nthr);
 }
 
 // Producer loop: for every item, `passes` sweeps over its token range (K then V
@@ -645,6 +776,7 @@ __global__ void __launch_bounds__(kPW * 32 + 32, 2) attn_polar_kernel(AttnParams
         named_bar_sync(1, nthr);
         finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, dim, tid, nthr, 4);
     }
+    xr_kernel_tail(p, tid, nthr);
 }
 
 // ---------------------------------------------------------------------------
@@ -932,6 +1064,7 @@ __global__ void __launch_bounds__(TMA ? kLW * 32 + 32 : kLW * 32) attn_lut_kerne
         named_bar_sync(1, nthr);
         finish_item(p, r, sM, sL, sO, sFin, sflag, sR, pitch, tid, nthr, 1);
     }
+    xr_kernel_tail(p, tid, nthr);
 }
 
 // ---------------------------------------------------------------------------
@@ -1020,6 +1153,7 @@ static int round_group(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
 #include "pkv_attn_tc.cu"
 #include "pkv_attn_mha8.cu"
 #include "pkv_attn_mha12.cu"
+#include "pkv_attn_gqa12.cu"
 
 namespace pkv {
 
@@ -1027,6 +1161,7 @@ struct AttnPlan {
     bool mha12;                        // attn_mha12_kernel, or with mha12s attn_mha12_stream_kernel
     bool mha12s;
     bool mha8;                         // attn_mha8_kernel
+    bool gqa12;                        // attn_gqa12_kernel: four query heads of one KV head per unit
     bool polar;                        // attn_polar_kernel, else attn_lut_kernel
     int G, TPL, stages, nsplit, chunk, tt, threads, smem, ctas_per_sm;
     bool tma;
@@ -1036,6 +1171,12 @@ struct AttnPlan {
     int tpu, seg_cap, slots;           // tiles per unit, tiles per segment at most, partial slots
     int64_t tiles, grid;               // balanced: total tiles, CTAs
 };
+
+// Work units per batch row: the KV heads; every query head (grouped heads on the one-head
+// kernels); or every four query heads (attn_gqa12_kernel).
+static int units_per_row(const AttnPlan& pl, const pkv_attn_args* a) {
+    return pl.qunits ? a->q_heads : pl.gqa12 ? a->q_heads / gqa12::HQ : a->kv_heads;
+}
 
 static bool tma_ok(const pkv_codec* c, const pkv_attn_args* a) {
     const int row_bytes = (c->dim / 3) * a->code_bytes;
@@ -1057,6 +1198,13 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     // grouped heads: every query head streams its KV head's codes on its own (the group's re-reads
     // of the same codes hit L2), which beats per-token work for the whole group at 12-bit codes
     pl.qunits = pl.mha12 && a->q_heads != a->kv_heads;
+    // groups of 4, 8, ... query heads: each code decoded once for four heads (measured on B200
+    // against one query head per unit, whose decode work grows with the group)
+    pl.gqa12 = pl.mha12 && a->q_heads / a->kv_heads >= gqa12::HQ && (a->q_heads / a->kv_heads) % gqa12::HQ == 0;
+    if (pl.gqa12) {
+        pl.mha12 = false;
+        pl.qunits = false;
+    }
     if (pl.mha12) {
         pl.G = 1;
         // measured on B200: the two-pass kernel wins while a unit is one item (phi3-decode,
@@ -1068,7 +1216,7 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
         const int n_xy = (c->xy_per_z ? Cz : 1) << (c->bits_r + c->bits_theta);
         // measured: grouped heads (one decode per KV token serves the whole group) and per-z-bin
         // tables gain on tensor cores; a single uniform-polar head is faster on the polar kernel
-        pl.tc = !pl.mha12 && pl.tma && c->dim == 96 && (a->q_dtype == PKV_BF16 || a->q_dtype == PKV_F16) &&
+        pl.tc = !pl.mha12 && !pl.gqa12 && pl.tma && c->dim == 96 && (a->q_dtype == PKV_BF16 || a->q_dtype == PKV_F16) &&
                 (a->code_bytes == 1 || a->code_bytes == 2) && n_xy <= 4096 && Cz <= 256 &&
                 a->q_heads / a->kv_heads <= 16 && (a->q_heads > a->kv_heads || c->xy_per_z != 0);
     }
@@ -1080,7 +1228,17 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
         pl.qunits = a->q_heads != a->kv_heads;
         pl.G = 1;
     }
-    if (pl.tc) {
+    if (pl.gqa12) {
+        pl.polar = false;
+        pl.TPL = 1;
+        pl.G = gqa12::HQ;
+        pl.tt = gqa12::TT;
+        pl.threads = gqa12::W * 32 + 32;
+        pl.stages = gqa12::SLOTS;
+        pl.smem = gqa12::TOTAL;
+        pl.chunk = 1 << 30;                // online softmax: no cap on the tokens of an item
+        pl.ctas_per_sm = 1;
+    } else if (pl.tc) {
         pl.polar = false;
         pl.TPL = 1;
         pl.tt = atc::TT;
@@ -1145,12 +1303,12 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     // split count: minimise rounds * (tiles per item + overhead); items carry at most `chunk` tokens
     const int tiles_total = std::max(1, (a->seq_len + pl.tt - 1) / pl.tt);
     const int max_tiles_item = std::max(1, pl.chunk / pl.tt);
-    const int64_t units = (int64_t)a->batch * (pl.qunits ? a->q_heads : a->kv_heads);
+    const int64_t units = (int64_t)a->batch * units_per_row(pl, a);
     const int64_t grid = (int64_t)num_sms() * pl.ctas_per_sm;
     // fixed cost of an item in tile units: the tensor-core kernel's items also rotate the group's
     // queries through global R and merge their splits, about eight of its 128-token tiles
     // (query rotation, score table and warp merge: about two tiles of the one-head kernels)
-    const double item_cost = pl.tc ? 8.0 : (pl.mha8 || pl.mha12s) ? 2.0 : 1.0;
+    const double item_cost = pl.tc ? 8.0 : pl.gqa12 ? 3.0 : (pl.mha8 || pl.mha12s) ? 2.0 : 1.0;
     int best = 0;
     double best_cost = 1e300;
     const int min_split = a->num_splits > 0 ? a->num_splits : (tiles_total + max_tiles_item - 1) / max_tiles_item;
@@ -1202,12 +1360,13 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
 bool attn_group_supported(const pkv_codec* c, const pkv_attn_args* a) {
     if (a->q_heads / a->kv_heads <= 8) return true;
     const AttnPlan pl = plan_attn(c, a);
-    return pl.tc || pl.mha12 || pl.mha8;
+    return pl.tc || pl.mha12 || pl.mha8 || pl.gqa12;
 }
 
 void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out) {
     const AttnPlan pl = plan_attn(c, a);
     out->kernel = pl.tc      ? PKV_KERNEL_TC
+                  : pl.gqa12 ? PKV_KERNEL_GQA12
                   : pl.mha12 ? (pl.mha12s ? PKV_KERNEL_MHA12_STREAM : PKV_KERNEL_MHA12)
                   : pl.mha8  ? PKV_KERNEL_MHA8
                              : (pl.polar ? PKV_KERNEL_POLAR : PKV_KERNEL_LUT);
@@ -1222,7 +1381,7 @@ void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* ou
 // Arrival counters of a split call: one per (batch row, unit head).
 size_t attn_counter_bytes(const pkv_codec* c, const pkv_attn_args* a) {
     const AttnPlan pl = plan_attn(c, a);
-    return (size_t)a->batch * (pl.qunits ? a->q_heads : a->kv_heads) * sizeof(int32_t);
+    return (size_t)a->batch * units_per_row(pl, a) * sizeof(int32_t);
 }
 
 size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a) {
@@ -1230,7 +1389,7 @@ size_t attn_workspace_size(const pkv_codec* c, const pkv_attn_args* a) {
     if (!pl.bal && pl.nsplit <= 1) return 0;
     size_t part = (size_t)a->batch * a->q_heads * pl.slots * (c->dim + 2) * sizeof(float);
     part = (part + 255) / 256 * 256;
-    return part + (size_t)a->batch * (pl.qunits ? a->q_heads : a->kv_heads) * sizeof(int32_t);
+    return part + (size_t)a->batch * units_per_row(pl, a) * sizeof(int32_t);
 }
 
 template <typename K>
@@ -1286,15 +1445,47 @@ static int launch_lut(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) 
     return pl.TPL == 1 ? launch_lut_tpl<CB, 1>(p, pl, st) : launch_lut_tpl<CB, 2>(p, pl, st);
 }
 
-int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st) {
+// Split-sequence exchange buffer of one rank: partial slots [world][rows][dim + 2], output rows
+// [rows][dim], one arrival counter per unit, then the done and CTA counters; 256-byte aligned parts.
+struct XrLayout { size_t out_off, cnt_off, done_off, bytes; int rows, units; };
+
+static XrLayout xr_layout_of(const pkv_codec* c, const pkv_attn_args* a, const AttnPlan& pl, int world) {
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    XrLayout L{};
+    L.rows = a->batch * a->q_heads;
+    L.units = a->batch * units_per_row(pl, a);
+    L.out_off = up((size_t)world * L.rows * (c->dim + 2) * sizeof(float));
+    L.cnt_off = L.out_off + up((size_t)L.rows * c->dim * sizeof(float));
+    L.done_off = L.cnt_off + up((size_t)L.units * sizeof(uint32_t));
+    L.bytes = L.done_off + 256;
+    return L;
+}
+
+void xr_layout(const pkv_codec* c, const pkv_attn_args* a, int world, pkv_xr_layout* out) {
+    const XrLayout L = xr_layout_of(c, a, plan_attn(c, a), world);
+    out->bytes = L.bytes;
+    out->out_offset = L.out_off;
+    out->rows = L.rows;
+    out->units = L.units;
+}
+
+// Byte offset and length of a rank's counters (the part pkv_xr_reset zeroes).
+void xr_counter_span(const pkv_codec* c, const pkv_attn_args* a, int world, size_t* off, size_t* len) {
+    const XrLayout L = xr_layout_of(c, a, plan_attn(c, a), world);
+    *off = L.cnt_off;
+    *len = L.bytes - L.cnt_off;
+}
+
+int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st,
+                const pkv_exchange* xr) {
     AttnPlan pl = plan_attn(c, a);
-    if (a->q_heads / a->kv_heads > 8 && !pl.tc && !pl.mha12 && !pl.mha8) return PKV_ERR_UNSUPPORTED;
+    if (a->q_heads / a->kv_heads > 8 && !pl.tc && !pl.mha12 && !pl.mha8 && !pl.gqa12) return PKV_ERR_UNSUPPORTED;
     if (pl.smem > 227 * 1024) return PKV_ERR_UNSUPPORTED;
     AttnParams p{};
     p.B = a->batch; p.Hq = a->q_heads; p.Hkv = a->kv_heads; p.S = a->seq_len;
-    p.G = pl.qunits ? 1 : a->q_heads / a->kv_heads; p.m = c->dim / 3; p.dim = c->dim;
-    p.Hu = pl.qunits ? a->q_heads : a->kv_heads;
-    p.Gq = pl.qunits ? a->q_heads / a->kv_heads : 1;
+    p.G = pl.qunits ? 1 : pl.gqa12 ? gqa12::HQ : a->q_heads / a->kv_heads; p.m = c->dim / 3; p.dim = c->dim;
+    p.Hu = units_per_row(pl, a);
+    p.Gq = pl.qunits ? a->q_heads / a->kv_heads : pl.gqa12 ? a->q_heads / a->kv_heads / gqa12::HQ : 1;
     p.q = a->q; p.qdt = a->q_dtype; p.q_bs = a->q_batch_stride; p.q_hs = a->q_head_stride;
     p.kc = static_cast<const uint8_t*>(a->k_codes); p.vc = static_cast<const uint8_t*>(a->v_codes);
     p.kv_bs = a->kv_batch_stride; p.kv_hs = a->kv_head_stride;
@@ -1325,6 +1516,19 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
     p.r_max = c->r_max;
     p.num_items = pl.bal ? (int)std::min<int64_t>(pl.tiles, INT32_MAX) : a->batch * p.Hu * pl.nsplit;
     p.stages = pl.stages;
+    if (xr) {
+        const XrLayout L = xr_layout_of(c, a, pl, xr->world);
+        p.xr_world = xr->world;
+        p.xr_rank = xr->rank;
+        p.xr_units = L.units;
+        for (int s = 0; s < xr->world; ++s) p.xr_buf[s] = static_cast<uint8_t*>(xr->buffers[s]);
+        p.xr_out_off = (int64_t)L.out_off;
+        p.xr_cnt_off = (int64_t)L.cnt_off;
+        p.xr_done_off = (int64_t)L.done_off;
+        p.xr_wait_ns = (uint64_t)xr->wait_limit_us * 1000ull;
+        p.partial_only = 0;
+        p.out = nullptr;
+    }
     if (p.num_items == 0) return PKV_OK;
     if (pl.tc) {
         if (a->code_bytes == 1)
@@ -1335,6 +1539,7 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
                          : pl.G == 8 ? launch_kernel(attn_tc_kernel<2, 8>, p, pl, st)
                                      : launch_kernel(attn_tc_kernel<2, 16>, p, pl, st);
     }
+    if (pl.gqa12) return launch_kernel(attn_gqa12_kernel, p, pl, st);
     if (pl.mha12s) return launch_kernel(attn_mha12_stream_kernel, p, pl, st);
     if (pl.mha12) return launch_kernel(attn_mha12_kernel, p, pl, st);
     if (pl.mha8) return launch_kernel(attn_mha8_kernel, p, pl, st);

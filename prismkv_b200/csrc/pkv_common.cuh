@@ -17,7 +17,8 @@ namespace pkv {
 // Device error word: set when a bounded wait expires; read by pkv_device_error.
 __device__ int32_t g_device_error = 0;   // single definition: the library is one translation unit
 
-enum : int32_t { kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3 };
+// 4: a split-sequence exchange waited past its bound for the other ranks' outputs
+enum : int32_t { kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3, kErrPeerWait = 4 };
 
 __device__ __forceinline__ void flag_error(int32_t code) { atomicCAS(&g_device_error, 0, code); }
 
@@ -200,6 +201,53 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// paired fp32 arithmetic on sm_100 with both values in one 64-bit register: the operands keep
+// that form from load to store, so no instruction splits or rebuilds the register pair
+// ---------------------------------------------------------------------------
+typedef unsigned long long f32x2;
+
+__device__ __forceinline__ f32x2 f2_pack(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ float2 f2_unpack(f32x2 v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+
+__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ f32x2 f2_mul(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 16 bytes of shared memory as two pairs; 8 bytes as one pair.
+__device__ __forceinline__ void lds_f2x2(uint32_t addr, f32x2& a, f32x2& b) {
+    asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
+}
+
+__device__ __forceinline__ f32x2 lds_f2(uint32_t addr) {
+    f32x2 v;
+    asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v) : "r"(addr));
+    return v;
 }
 
 __device__ __forceinline__ float fast_exp2(float x) {

@@ -103,6 +103,17 @@ def _kv_rows(w: Workload, g: torch.Generator, device, rows: int, head_of_row: to
     return x
 
 
+def _workload_layout(w: Workload, device) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor]]:
+    """The per-KV-head scales and the outlier channels of a workload (fixed across seeds)."""
+    gh = torch.Generator().manual_seed(1)
+    scales = (0.5 + 1.5 * torch.rand(w.kv_heads, generator=gh)).to(device) if w.head_scale else None
+    outlier = None
+    if w.outliers:
+        n_out = max(1, round(0.01 * w.dim))
+        outlier = torch.randperm(w.dim, generator=gh)[:n_out].to(device)
+    return scales, outlier
+
+
 def make_kv_codes(w: Workload, quantizer: StackedPlaneQuantizer, device, seed: int = 0,
                   chunk_rows: int = 1 << 21) -> Tuple[torch.Tensor, torch.Tensor]:
     """(B, Hkv, S, m) packed K and V codes: Gaussian vectors encoded on the GPU in chunks.
@@ -113,12 +124,7 @@ def make_kv_codes(w: Workload, quantizer: StackedPlaneQuantizer, device, seed: i
     """
     device = torch.device(device)
     g = torch.Generator(device=device).manual_seed(seed)
-    gh = torch.Generator().manual_seed(1)
-    scales = (0.5 + 1.5 * torch.rand(w.kv_heads, generator=gh)).to(device) if w.head_scale else None
-    outlier = None
-    if w.outliers:
-        n_out = max(1, round(0.01 * w.dim))
-        outlier = torch.randperm(w.dim, generator=gh)[:n_out].to(device)
+    scales, outlier = _workload_layout(w, device)
     codec = quantizer.codec(device)
     shape = (w.batch, w.kv_heads, w.seq_len, w.m)
     dt = quantizer.code_dtype

@@ -1,6 +1,7 @@
 """bench.py's reference arm runs on the host's cores and prints one JSON line with the
 benchmark contract's keys (impl, metric, value, unit, cpu_baseline, e2e with zero copy
-bytes), on the workload the GPU arm measures."""
+bytes), on the workload the GPU arm measures; with the reference installed in baseline/_ref
+it times the reference's own code."""
 
 import json
 import os
@@ -20,9 +21,11 @@ def test_reference_arm_prints_one_contract_line():
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] == 3
     assert d["unit"] == "GB/s" and d["value"] > 0 and d["higher_is_better"] is True
-    assert d["config"]["workload"] == "phi3-decode"
+    assert d["config"]["workload"] == "longctx-splitseq"
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == d["value"]
+    if os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "prismkv")):
+        assert cb["kind"] == "reference" and "PolarAttentionApprox.forward" in cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 

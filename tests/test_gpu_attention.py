@@ -101,7 +101,13 @@ CASES = [
     (2, 8, 4, 2000, "v1", (4, 4, 4), torch.float32, 16),
     (1, 8, 8, 5000, "v1", (4, 4, 4), torch.float32, 0),           # past 4096 tokens: one-pass 12-bit kernel
     (2, 8, 8, 4097, "v1", (4, 4, 4), torch.bfloat16, 0),
-    (1, 32, 8, 9000, "v1", (4, 4, 4), torch.float32, 0),          # grouped, one query head per unit
+    (1, 32, 8, 9000, "v1", (4, 4, 4), torch.float32, 0),          # group 4: four heads per unit
+    (2, 16, 4, 3000, "v1", (4, 4, 4), torch.bfloat16, 0),         # group 4, bf16 queries
+    (1, 8, 2, 777, "v1", (4, 4, 4), torch.float16, 0),            # group 4, partial tiles
+    (2, 32, 4, 5000, "v1", (4, 4, 4), torch.float32, 0),          # group 8: two units per KV head
+    (1, 16, 4, 20000, "v1", (4, 4, 4), torch.float32, 3),         # group 4, forced splits
+    (1, 4, 1, 1, "v1", (4, 4, 4), torch.float32, 0),              # group 4, one token
+    (1, 64, 4, 600, "v1", (4, 4, 4), torch.bfloat16, 0),          # group 16
     (1, 8, 8, 12345, "v1", (4, 4, 4), torch.float16, 5),
 ]
 
@@ -131,11 +137,12 @@ def test_attention_other_head_dims(cuda_ready, dim):
     np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
 
 
-@pytest.mark.parametrize("bits,S", [((4, 4, 4), 512), ((3, 3, 2), 512), ((4, 4, 4), 6000)])
-def test_attention_ragged_and_empty_rows(cuda_ready, bits, S):
+@pytest.mark.parametrize("bits,S,Hq", [((4, 4, 4), 512, 8), ((3, 3, 2), 512, 8), ((4, 4, 4), 6000, 8),
+                                       ((4, 4, 4), 6000, 32)])
+def test_attention_ragged_and_empty_rows(cuda_ready, bits, S, Hq):
     q, p = _setup("v1", bits)
     kc, vc = _codes(q, 3, 8, S, seed=2)
-    qv = torch.randn(3, 8, 96, generator=torch.Generator(device=DEV).manual_seed(2), device=DEV)
+    qv = torch.randn(3, Hq, 96, generator=torch.Generator(device=DEV).manual_seed(2), device=DEV)
     lens = torch.tensor([S, 0, 77 if S < 1000 else 4500], dtype=torch.int32, device=DEV)
     for splits in (0, 1, 3):
         out = decode_attention(q, qv, kc, vc, seq_lens=lens, num_splits=splits)
@@ -158,25 +165,30 @@ def test_attention_capacity_strided_cache(cuda_ready):
     np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
 
 
-def test_attention_partials_and_lse_combine(cuda_ready):
-    """Shard the sequence (uneven, one empty shard), keep partials, merge: equals unsplit."""
+@pytest.mark.parametrize("Hq,H", [(8, 8), (32, 8)])
+def test_attention_partials_and_lse_combine(cuda_ready, Hq, H):
+    """Shard the sequence (uneven, one empty shard), keep partials, merge: equals unsplit.
+    MHA runs the one-head 12-bit kernel, groups of four the grouped kernel."""
     q, p = _setup("v1", (4, 4, 4))
-    B, H, S = 2, 8, 1500
+    B, S = 2, 1500
+    G = Hq // H
     kc, vc = _codes(q, B, H, S, seed=4)
-    qv = torch.randn(B, H, 96, generator=torch.Generator(device=DEV).manual_seed(4), device=DEV)
+    qv = torch.randn(B, Hq, 96, generator=torch.Generator(device=DEV).manual_seed(4), device=DEV)
     codec = q.codec(torch.device(DEV))
     bounds = [0, 700, 700, 1500]
     parts = []
     for a, b in zip(bounds[:-1], bounds[1:]):
-        parts.append(codec.attention(qv, kc[:, :, a:b], vc[:, :, a:b], partial=True).view(B * H, 98))
-    merged = codec.combine(torch.stack(parts)).view(B, H, 96)
+        parts.append(codec.attention(qv, kc[:, :, a:b], vc[:, :, a:b], partial=True).view(B * Hq, 98))
+    merged = codec.combine(torch.stack(parts)).view(B, Hq, 96)
     ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64), vc.cpu().numpy().astype(np.int64),
                            q.R.numpy(), p)
     np.testing.assert_allclose(merged.cpu().numpy(), ref, atol=TOL, rtol=0)
     # partial contents against an fp64 restatement (natural-log max, l, o in rotated space)
-    pa = parts[0].view(B, H, 98).cpu().numpy().astype(np.float64)
+    pa = parts[0].view(B, Hq, 98).cpu().numpy().astype(np.float64)
     kr = oracle.dequant_rotated(kc[:, :, :700].cpu().numpy().reshape(-1, 32), p).reshape(B, H, 700, 96)
     vr = oracle.dequant_rotated(vc[:, :, :700].cpu().numpy().reshape(-1, 32), p).reshape(B, H, 700, 96)
+    kr = np.repeat(kr, G, axis=1)
+    vr = np.repeat(vr, G, axis=1)
     qr = qv.cpu().numpy().astype(np.float64) @ q.R.numpy().astype(np.float64).T
     s = np.einsum("bhd,bhsd->bhs", qr, kr) * 96 ** -0.5
     mx = s.max(-1)
@@ -184,7 +196,7 @@ def test_attention_partials_and_lse_combine(cuda_ready):
     np.testing.assert_allclose(pa[..., 0], mx, atol=1e-4)
     np.testing.assert_allclose(pa[..., 1], w.sum(-1), rtol=1e-4)
     np.testing.assert_allclose(pa[..., 2:], np.einsum("bhs,bhsd->bhd", w, vr), rtol=1e-4, atol=1e-3)
-    empty = parts[1].view(B, H, 98)
+    empty = parts[1].view(B, Hq, 98)
     assert torch.isinf(empty[..., 0]).all() and (empty[..., 1:] == 0).all()
 
 
@@ -219,9 +231,10 @@ def test_attention_shapes_in_turn_share_workspace(cuda_ready):
 
 @pytest.mark.parametrize("B,Hq,Hkv,S,variant,bits,kernel", [
     (8, 32, 32, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),
-    (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),        # grouped heads, one query head per unit
+    (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_gqa12_kernel"),        # grouped heads: four per unit
+    (4, 16, 8, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),        # group 2: one query head per unit
     (1, 8, 8, 4097, "v1", (4, 4, 4), "attn_mha12_stream_kernel"),
-    (4, 32, 8, 131072, "v1", (4, 4, 4), "attn_mha12_stream_kernel"),
+    (4, 32, 8, 131072, "v1", (4, 4, 4), "attn_gqa12_kernel"),
     (2, 8, 8, 4096, "v1", (3, 3, 2), "attn_mha8_kernel"),
     (2, 32, 8, 4096, "v1", (3, 3, 2), "attn_mha8_kernel"),        # fp32 queries of a group
     (2, 8, 8, 4096, "v1", (2, 3, 3), "attn_polar_kernel"),
@@ -286,3 +299,46 @@ def test_aggressive_decode_full_size(cuda_ready):
     ref = oracle.attention(qv[rows].float().cpu().numpy(), kc[rows].cpu().numpy().astype(np.int64),
                            vc[rows].cpu().numpy().astype(np.int64), q.R.numpy(), p)
     np.testing.assert_allclose(out[rows].cpu().numpy(), ref, atol=TOL, rtol=0)
+
+
+def test_longctx_full_size_with_outliers(cuda_ready):
+    """The split-sequence workload at full size on one GPU (B=4, 32 query / 8 KV heads, S=131072,
+    1 % of the channels x8 before the rotation) through the grouped 12-bit kernel; two (batch,
+    KV head) units -- eight query heads -- against the oracle at the fp32 bound."""
+    from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
+    w = WORKLOADS["longctx-splitseq"]
+    q = make_quantizer(w)
+    kc, vc = make_kv_codes(w, q, DEV)
+    qv = make_query(w, DEV)
+    assert q.codec(torch.device(DEV)).describe(qv, kc, vc)["kernel"] == "attn_gqa12_kernel"
+    out = decode_attention(q, qv, kc, vc)
+    p = oracle.QuantParams.default(96)
+    for b, hk in ((0, 0), (3, 7)):
+        ref = oracle.attention(qv[b:b + 1, 4 * hk:4 * hk + 4].float().cpu().numpy(),
+                               kc[b:b + 1, hk:hk + 1].cpu().numpy().astype(np.int64),
+                               vc[b:b + 1, hk:hk + 1].cpu().numpy().astype(np.int64), q.R.numpy(), p)
+        np.testing.assert_allclose(out[b:b + 1, 4 * hk:4 * hk + 4].cpu().numpy(), ref, atol=TOL, rtol=0)
+    from prismkv_b200 import _lib
+    assert _lib.device_error() == 0
+
+
+def test_learned_gqa_full_size(cuda_ready):
+    """The learned-codebook workload at full size (B=16, 32 query / 8 KV heads, S=32768, 16x256
+    codebooks + BiasTable, bf16 queries) on the tensor-core kernel; two units against the oracle at
+    the bf16 bound."""
+    from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
+    w = WORKLOADS["learned-gqa"]
+    q = make_quantizer(w)
+    kc, vc = make_kv_codes(w, q, DEV)
+    qv = make_query(w, DEV)
+    assert q.codec(torch.device(DEV)).describe(qv, kc, vc)["kernel"] == "attn_tc_kernel"
+    out = decode_attention(q, qv, kc, vc)
+    p = oracle.QuantParams.default(96)
+    p.codebook = q._codebooks.codebooks.numpy()
+    p.bias_table = q._bias.table.numpy()
+    p.bias_delta_z = q._bias.delta_z
+    for b, hk in ((0, 0), (15, 5)):
+        ref = oracle.attention(qv[b:b + 1, 4 * hk:4 * hk + 4].float().cpu().numpy(),
+                               kc[b:b + 1, hk:hk + 1].cpu().numpy().astype(np.int64),
+                               vc[b:b + 1, hk:hk + 1].cpu().numpy().astype(np.int64), q.R.numpy(), p)
+        np.testing.assert_allclose(out[b:b + 1, 4 * hk:4 * hk + 4].cpu().numpy(), ref, atol=TOL_TC, rtol=0)

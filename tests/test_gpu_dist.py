@@ -1,5 +1,5 @@
-"""Split-sequence (NCCL all-gather, and symmetric-memory peer reads) and batch-sharded
-decode on 2 GPUs, against the oracle.
+"""Split-sequence (NCCL all-gather, and the in-kernel exchange over CUDA-IPC peer memory) and
+batch-sharded decode on 2 GPUs, against the oracle.
 
 Runs only where at least two GPUs are visible; the exchange logic itself is
 also covered on CPU with gloo (test_dist_cpu.py).  NVLS is off in these child
@@ -27,14 +27,14 @@ def _worker(rank, world, port, results):
     try:
         import oracle
         from prismkv_b200 import StackedPlaneQuantizer
-        from prismkv_b200.dist import PeerExchange, batch_shard_decode, shard_range, split_sequence_decode
+        from prismkv_b200.dist import SequenceExchange, batch_shard_decode, shard_range, split_sequence_decode
         err_seq = err_batch = 0.0
-        exchanges = []                               # kept alive until every rank is done reading
-        # shards on the two-pass 12-bit kernel, the one-pass 12-bit kernel (shards past 4096
-        # tokens) and the one-byte kernel, all in partial mode for the sequence split
-        for bits, S in (((4, 4, 4), 3001), ((4, 4, 4), 9001), ((3, 3, 2), 5001)):
+        # shards on the grouped 12-bit kernel, the two-pass and one-pass one-head 12-bit kernels
+        # (MHA shards below and past 4096 tokens) and the one-byte kernel
+        for bits, S, Hq, Hkv in (((4, 4, 4), 3001, 16, 4), ((4, 4, 4), 5001, 8, 8), ((4, 4, 4), 9001, 8, 8),
+                                 ((3, 3, 2), 5001, 16, 4)):
             q = StackedPlaneQuantizer(96, *bits, seed=42)
-            B, Hq, Hkv = 2, 16, 4
+            B = 2
             g = torch.Generator().manual_seed(9)
             k = torch.randn(B * Hkv * S, 96, generator=g)
             v = torch.randn(B * Hkv * S, 96, generator=g)
@@ -47,12 +47,13 @@ def _worker(rank, world, port, results):
             ref = oracle.attention(qv.cpu().numpy(), kc.cpu().numpy().astype(np.int64),
                                    vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
             err_seq = max(err_seq, float(np.abs(out.cpu().numpy() - ref).max()))
-            ex = PeerExchange(B * Hq, 96, dev)
-            exchanges.append(ex)
-            for _ in range(3):                       # both buffer halves, then the first again
-                outp = split_sequence_decode(q, qv, kc[:, :, a:b].contiguous(), vc[:, :, a:b].contiguous(),
-                                             exchange=ex)
+            ks, vs = kc[:, :, a:b].contiguous(), vc[:, :, a:b].contiguous()
+            ex = SequenceExchange(q, qv, ks, wait_ms=5000)
+            for _ in range(3):                       # the counters reset themselves between steps
+                outp = split_sequence_decode(q, qv, ks, vs, exchange=ex)
+                ex.check()
                 err_seq = max(err_seq, float(np.abs(outp.cpu().numpy() - ref).max()))
+            ex.close()
             ba, bb = shard_range(B, world, rank)
             outb = batch_shard_decode(q, qv[ba:bb].contiguous(), kc[ba:bb].contiguous(), vc[ba:bb].contiguous())
             err_batch = max(err_batch, float(np.abs(outb.cpu().numpy() - ref[ba:bb]).max()))

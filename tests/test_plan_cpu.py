@@ -53,7 +53,11 @@ BF16 = _lib.PKV_BF16
     ("phi3-decode", {}, (8, 32, 32, 4096, (4, 4, 4), BF16), "attn_mha12_kernel"),
     ("aggressive-332", dict(bits=(3, 3, 2)), (32, 32, 32, 16384, (3, 3, 2), BF16), "attn_mha8_kernel"),
     ("learned-gqa", dict(learned=True, bias=True), (16, 32, 8, 32768, (4, 4, 4), BF16), "attn_tc_kernel"),
-    ("longctx-splitseq", {}, (4, 32, 8, 131072, (4, 4, 4), BF16), "attn_mha12_stream_kernel"),
+    ("longctx-splitseq", {}, (4, 32, 8, 131072, (4, 4, 4), BF16), "attn_gqa12_kernel"),
+    ("longctx, one rank of eight", {}, (4, 32, 8, 16384, (4, 4, 4), BF16), "attn_gqa12_kernel"),
+    ("group 8, 12-bit, fp32", {}, (2, 16, 2, 3000, (4, 4, 4), _lib.PKV_F32), "attn_gqa12_kernel"),
+    ("group 2, 12-bit: one query head per unit", {}, (2, 8, 4, 3000, (4, 4, 4), BF16), "attn_mha12_kernel"),
+    ("group 2, long: one query head per unit", {}, (2, 8, 4, 9000, (4, 4, 4), BF16), "attn_mha12_stream_kernel"),
     ("cpu-roundtrip", {}, (1, 8, 8, 1024, (4, 4, 4), _lib.PKV_F32), "attn_mha12_kernel"),
     ("learned, fp32 queries", dict(learned=True, bias=True), (2, 32, 8, 4096, (4, 4, 4), _lib.PKV_F32),
      "attn_lut_kernel"),
@@ -86,7 +90,14 @@ def test_planner_honours_forced_splits():
 
 
 def test_one_head_kernels_fill_the_grid():
-    """One CTA per SM for the one-byte kernel, two for the 12-bit kernels."""
+    """One CTA per SM for the one-byte and the grouped 12-bit kernels, two for the one-head 12-bit kernels."""
     assert _plan(_codec(bits=(3, 3, 2)), _args(32, 32, 32, 16384, (3, 3, 2), BF16)).ctas_per_sm == 1
     assert _plan(_codec(), _args(8, 32, 32, 4096, (4, 4, 4), BF16)).ctas_per_sm == 2
-    assert _plan(_codec(), _args(4, 32, 8, 131072, (4, 4, 4), BF16)).ctas_per_sm == 2
+    assert _plan(_codec(), _args(8, 32, 32, 8192, (4, 4, 4), BF16)).ctas_per_sm == 2
+    assert _plan(_codec(), _args(4, 32, 8, 131072, (4, 4, 4), BF16)).ctas_per_sm == 1
+
+
+def test_grouped_12bit_kernel_streams_balanced_ranges():
+    """longctx (32 units of 131072 tokens on 148 SMs): every CTA streams an equal share of tiles."""
+    p = _plan(_codec(), _args(4, 32, 8, 131072, (4, 4, 4), BF16))
+    assert p.balanced == 1 and p.smem_bytes <= 227 * 1024 and p.threads == 20 * 32
