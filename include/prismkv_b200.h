@@ -212,10 +212,11 @@ PKV_API int pkv_attn_describe(const pkv_codec *c, const pkv_attn_args *a, pkv_at
  * split's arrival counters -- batch * kv_heads, or batch * q_heads when
  * grouped heads of 12-bit codes run one query head per unit -- must not
  * exceed PKV_NOALLOC_MAX_KV_ROWS; otherwise PKV_ERR_SCRATCH_LIMIT and
- * nothing is launched.  The first
- * call on a device resolves the array's address (cudaGetSymbolAddress, with
- * that device current) and zeroes its counter region on `stream`; make it
- * before any stream capture.  The counters must be zero when a kernel starts;
+ * nothing is launched.  Every call
+ * looks the array's address up for the current context (cudaGetSymbolAddress,
+ * with the device current); the first call that sees an address on a device
+ * also zeroes its counter region on `stream` -- make that call before any
+ * stream capture.  The counters must be zero when a kernel starts;
  * each call leaves them zero.  The array is shared: calls that overlap in
  * time on one device (other streams, unsynchronised threads) race on it.   */
 #define PKV_NOALLOC_SCRATCH_BYTES (8u << 20)
@@ -253,11 +254,10 @@ PKV_API int pkv_lse_combine_gather(const pkv_codec *c, const float *const *part_
  * On expiry it sets the device error word to 4 (read by pkv_device_error) and
  * returns; the counters are then left as they were, and every rank must call
  * pkv_xr_reset (after a host-side agreement that the step failed) before the
- * next step.  No
- * multicast object is involved: buffers come from cudaMalloc and are mapped
- * into the peers with CUDA IPC.  Replaces the reference's nothing: the
- * reference decodes on one CPU (polar_attention.py:277-309); sharding the
- * sequence is the decomposition of that same softmax.
+ * next step.  The buffers are plain cudaMalloc memory (no NVSwitch object)
+ * mapped into the peers with CUDA IPC.  The reference has no counterpart: it
+ * decodes on one CPU (polar_attention.py:277-309); sharding the sequence is
+ * the decomposition of that same softmax.
  *
  * Buffer layout (pkv_xr_layout): partial slots [world][rows][dim + 2] f32,
  * output rows [rows][dim] f32 (rows = batch * q_heads, row b * q_heads + h),

@@ -35,6 +35,5 @@ class PrismKVConfig:
         return 16 / self.bits_per_dim
 
     def __repr__(self) -> str:
-        return (f"PrismKVConfig(bits_z={self.bits_z}, bits_r={self.bits_r}, "
-                f"bits_theta={self.bits_theta}, {self.bits_per_dim:.1f} bits/dim, "
-                f"{self.compression_vs_fp16:.1f}× vs FP16)")
+        return (f"<PrismKVConfig {self.bits_z}+{self.bits_r}+{self.bits_theta} bits per triplet: "
+                f"{self.bits_per_dim:.2f} bits/dim, {self.compression_vs_fp16:.2f}x smaller than fp16>")

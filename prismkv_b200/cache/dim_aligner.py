@@ -26,5 +26,5 @@ class DimAligner:
         return x if self.pad_width == 0 else x[..., : self.original_dim]
 
     def __repr__(self) -> str:
-        return (f"DimAligner(original_dim={self.original_dim}, padded_dim={self.padded_dim}, "
-                f"waste={self.pad_width / self.padded_dim * 100:.1f}%)")
+        return (f"<DimAligner {self.original_dim} -> {self.padded_dim} dims "
+                f"({self.pad_width} zero pad)>")

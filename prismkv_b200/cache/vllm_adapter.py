@@ -12,7 +12,7 @@ the codes back and decodes them on the GPU.
 
 from __future__ import annotations
 
-from typing import Dict, Optional, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
@@ -41,29 +41,71 @@ class VLLMSwapCompressor:
         self._backends: Dict[int, PrismKVBackend] = {
             i: PrismKVBackend(self._config, head_dim=head_dim, device=device) for i in range(n_layers)}
         self._compressed: Dict[Tuple[int, int], Tuple[torch.Tensor, torch.Tensor]] = {}
+        # pinned host buffers of evicted blocks, reused by size: a swap loop allocates pinned
+        # memory only until the pool covers its working set
+        self._pool: Dict[Tuple[int, ...], List[torch.Tensor]] = {}
+        # device -> host copies not yet known to be complete: (block key, event)
+        self._pending: Dict[Tuple[int, int], torch.cuda.Event] = {}
+
+    def _host_buffer(self, shape) -> torch.Tensor:
+        free = self._pool.get(tuple(shape))
+        if free:
+            return free.pop()
+        return torch.empty(shape, dtype=torch.int16, pin_memory=True)
 
     def compress_block(self, layer_idx: int, block_id: int, k_block: torch.Tensor,
-                       v_block: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+                       v_block: torch.Tensor, sync: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
         """(num_heads, block_size, head_dim) blocks -> (num_heads * block_size, n_groups) int16 codes
-        stored on the compressor's device."""
+        stored on the compressor's device.
+
+        With host storage the codes go to pinned buffers (reused from evicted blocks) by an
+        asynchronous copy.  ``sync=True`` (the reference's behaviour) waits for this block's
+        copies before returning; ``sync=False`` returns at once -- the codes are complete after
+        ``synchronize()``, and ``decompress_block`` of the block on the same stream needs no wait.
+        """
         n_heads, block_size, head_dim = k_block.shape
         N = n_heads * block_size
         backend = self._backends[layer_idx]
         dev = _cuda_device(k_block)
         codec = backend.codec(dev)
+        key = (layer_idx, block_id)
         out = []
         for blk in (k_block, v_block):
             x = backend.aligner.pad(blk.to(dev).reshape(N, head_dim))
             codes = codec.encode(x, code_dtype=torch.int16)
             if torch.device(self._device).type == "cpu":
-                host = torch.empty(codes.shape, dtype=codes.dtype, pin_memory=True)
+                host = self._host_buffer(codes.shape)
                 host.copy_(codes, non_blocking=True)
                 out.append(host)
             else:
                 out.append(codes.to(self._device))
-        torch.cuda.current_stream(dev).synchronize()
-        self._compressed[(layer_idx, block_id)] = (out[0], out[1])
+        if torch.device(self._device).type == "cpu":
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(dev))
+            if sync:
+                ev.synchronize()
+            else:
+                self._pending[key] = ev
+        self._release(key)
+        self._compressed[key] = (out[0], out[1])
         return out[0], out[1]
+
+    def synchronize(self) -> None:
+        """Wait until every block compressed with ``sync=False`` is in host memory."""
+        for ev in self._pending.values():
+            ev.synchronize()
+        self._pending.clear()
+
+    def _release(self, key) -> None:
+        """Return a block's pinned buffers to the pool (after its copies are done)."""
+        old = self._compressed.pop(key, None)
+        ev = self._pending.pop(key, None)
+        if ev is not None:
+            ev.synchronize()
+        if old is not None and torch.device(self._device).type == "cpu":
+            for t in old:
+                if t.is_pinned():
+                    self._pool.setdefault(tuple(t.shape), []).append(t)
 
     def decompress_block(self, layer_idx: int, block_id: int, n_heads: int, block_size: int,
                          dtype: torch.dtype = torch.float16, device: str = "cuda") -> Tuple[torch.Tensor, torch.Tensor]:
@@ -85,8 +127,8 @@ class VLLMSwapCompressor:
         return out[0], out[1]
 
     def evict_block(self, layer_idx: int, block_id: int) -> None:
-        """Drop a compressed block (the block was freed in vLLM)."""
-        self._compressed.pop((layer_idx, block_id), None)
+        """Drop a compressed block (the block was freed in vLLM); its pinned buffers are reused."""
+        self._release((layer_idx, block_id))
 
     def attach(self, engine: object) -> None:
         """Wrap ``engine.cache_engine`` swap_out / swap_in (vLLM 0.4-0.6 CacheEngine API).
@@ -117,5 +159,5 @@ class VLLMSwapCompressor:
         return len(self._compressed)
 
     def __repr__(self) -> str:
-        return (f"VLLMSwapCompressor(head_dim={self._head_dim}, n_layers={self._n_layers}, "
-                f"{self._config.bits_per_dim:.1f}bits/dim, compressed_blocks={len(self._compressed)})")
+        return (f"<VLLMSwapCompressor head_dim {self._head_dim}, {self._n_layers} layers, "
+                f"{len(self._compressed)} blocks held>")

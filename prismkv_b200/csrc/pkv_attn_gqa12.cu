@@ -38,12 +38,14 @@ constexpr int HQ = 4;                                   // query heads per unit
 constexpr int TW = 16;                                  // tokens per warp per tile
 constexpr int TT = W * TW;                              // tokens per tile
 constexpr int HALF = TT * 64;                           // K (or V) codes of a tile: 32 x uint16 / token
-constexpr int SLOTS = 4;                                // ring of half tiles
+constexpr int SLOTS = 3;                                // ring of half tiles
 constexpr int KT_HALF = 256 * 16 * 16;                  // [256 flat][16 slots] float4
 constexpr int KT_BYTES = 2 * KT_HALF;
 constexpr int OFF_KT = 0;
 constexpr int OFF_RING = OFF_KT + KT_BYTES;
-constexpr int OFF_CS = OFF_RING + SLOTS * HALF;         // [16] float2, 128-byte aligned
+constexpr int XY_COPIES = 8;                            // V's (x, y) table, one copy per 2 lane columns
+constexpr int OFF_XY = OFF_RING + SLOTS * HALF;         // [256 flat][8 copies] float2: (x, y) of the flat index
+constexpr int OFF_CS = OFF_XY + 256 * XY_COPIES * 8;    // [16] float2, 128-byte aligned
 constexpr int OFF_Q = OFF_CS + 128;                     // [4][96] rotated, scaled queries
 constexpr int OFF_QRAW = OFF_Q + HQ * 96 * 4;           // [4][96] raw queries
 constexpr int OFF_P = OFF_QRAW + HQ * 96 * 4;           // [W][TW tokens][2] float4 weight pairs
@@ -55,8 +57,10 @@ constexpr int TOTAL = OFF_BAR + 2 * SLOTS * 8;
 constexpr int OFF_ACC = OFF_KT;                         // item merge [W][4][96] over the dead table
 constexpr float MAGIC = 8388608.f;                      // 2^23
 static_assert(W * HQ * 96 * 4 <= KT_BYTES, "merge buffer fits the table region");
-static_assert(OFF_RING % 128 == 0 && OFF_CS % 128 == 0 && OFF_P % 16 == 0 && OFF_BAR % 8 == 0, "alignment");
+static_assert(OFF_RING % 128 == 0 && OFF_XY % 128 == 0 && OFF_CS % 128 == 0 && OFF_P % 16 == 0 &&
+              OFF_BAR % 8 == 0, "alignment");
 static_assert(TOTAL <= 227 * 1024, "one CTA per SM");
+static_assert(W * 32 >= HQ * 96, "one consumer thread per query element (the query prefetch)");
 }  // namespace gqa12
 
 __device__ __forceinline__ uint2 lds_u32x2(uint32_t addr) {
@@ -80,7 +84,8 @@ __device__ __forceinline__ float4 lds_f32x4(uint32_t addr) {
 // Producer: half tiles in consumption order (K of tile t, then V of tile t) into the ring.
 __device__ void produce_gqa12(const AttnParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty) {
     using namespace gqa12;
-    int seq = 0;
+    int seq = 0, s = 0;
+    uint32_t phase = 0;                                   // phase of slot s's next fill
     bool ok = true;
     WorkCursor wc = work_begin(p);
     ItemRange r;
@@ -90,11 +95,12 @@ __device__ void produce_gqa12(const AttnParams& p, uint8_t* ring, uint64_t* full
             const uint32_t bytes = (uint32_t)min(TT, r.tok1 - t0) * 64u;
             const int64_t off = base + (int64_t)t0 * 64;
             #pragma unroll 1
-            for (int h = 0; h < 2; ++h, ++seq) {
-                const int s = seq % SLOTS, use = seq / SLOTS;
-                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, kErrWaitEmpty)) { ok = false; break; }
+            for (int h = 0; h < 2; ++h) {
+                if (seq >= SLOTS && !mbar_wait(&empty[s], phase ^ 1u, kErrWaitEmpty)) { ok = false; break; }
                 mbar_arrive_expect_tx(&full[s], bytes);
                 bulk_g2s(ring + s * HALF, (h ? p.vc : p.kc) + off, bytes, &full[s]);
+                ++seq;
+                if (++s == SLOTS) { s = 0; phase ^= 1u; }
             }
         }
     }
@@ -140,6 +146,19 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
         }
         fence_mbar_init();
     }
+    // V's (x, y) table: row e = (i_r << 4) | i_theta holds XY_COPIES copies of (16 i_r) * vCS[i_theta]
+    // (the same product as the radius times the (cos, sin) table), copy k at bytes 8k of the row:
+    // lanes c and c + 8 share copy c & 7, two lanes (of the two tokens a load serves) per bank pair
+    {
+        float2* xy = reinterpret_cast<float2*>(smem + OFF_XY);
+        const float drs = dr * 0.0625f;
+        for (int i = tid; i < 256 * XY_COPIES; i += blockDim.x) {
+            const int e = i / XY_COPIES;
+            const float th = (float)(e & 15) / 15.f * 6.283185307179586f - 3.141592653589793f;
+            const float rr = (float)(e & 0xF0);
+            xy[i] = make_float2(rr * (cosf(th) * drs), rr * (sinf(th) * drs));
+        }
+    }
     float qreg = 0.f;                                     // the first item's queries, ahead of the stream
     {
         WorkCursor pc = work_begin(p);
@@ -163,7 +182,8 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
     const uint32_t kt_g = 16u * g;                        // byte 0 of a table address: this lane's slot
     const uint32_t csb = smem_base + OFF_CS;
     float4* pbuf = reinterpret_cast<float4*>(smem + OFF_P) + warp * TW * 2;
-    int seq = 0;
+    int slot = 0;                                        // ring slot of the next half tile, its fill phase
+    uint32_t phase = 0;
     bool alive = true;
     WorkCursor wc = work_begin(p);
     ItemRange r;
@@ -199,9 +219,9 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
         // score table, two halves of [256 flat][16 slots] float4: triplet j = 4 g + i lives in half
         // i >> 1, slot 8 (i & 1) + g, so a lane's four triplets are at fixed offsets from
         // flat * 256 + 16 g and the eight lane groups of one load hit eight distinct bank groups.
-        // Thread t < 512 fills triplet j = t & 31, theta index e0 = t >> 5, rows e0 + 16 i_r.
-        if (tid < 512) {
-            const int j = tid & 31, e0 = tid >> 5;
+        // Index t < 512 fills triplet j = t & 31, theta index e0 = t >> 5, rows e0 + 16 i_r.
+        for (int t = tid; t < 512; t += nthr) {
+            const int j = t & 31, e0 = t >> 5;
             const float2 cs = vCS[e0];
             float A[HQ];
             #pragma unroll
@@ -248,8 +268,8 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
             const int nt = min(TT, ntok - tile * TT);
             const int wt0 = warp * TW;                      // this warp's first token of the tile
             // ---- K: scores of 16 tokens x 4 heads ----------------------------------------
-            int s = seq % SLOTS;
-            if (alive && !mbar_wait(&full[s], (seq / SLOTS) & 1, kErrWaitFull)) alive = false;
+            int s = slot;
+            if (alive && !mbar_wait(&full[s], phase, kErrWaitFull)) alive = false;
             const bool act = alive && wt0 < nt;
             float2 sc = make_float2(-INFINITY, -INFINITY);
             if (act) {
@@ -315,7 +335,7 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
-            ++seq;
+            if (++slot == SLOTS) { slot = 0; phase ^= 1u; }
             // ---- online softmax per head ------------------------------------------------
             if (act) {
                 if (__any_sync(0xffffffffu, sc.x > mp.x || sc.y > mp.y)) {      // rare after the first tiles
@@ -347,11 +367,12 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
             }
             __syncwarp();
             // ---- V: weighted sums of 16 tokens for 4 heads -------------------------------
-            s = seq % SLOTS;
-            if (alive && !mbar_wait(&full[s], (seq / SLOTS) & 1, kErrWaitFull)) alive = false;
+            s = slot;
+            if (alive && !mbar_wait(&full[s], phase, kErrWaitFull)) alive = false;
             if (act && alive) {
                 const uint32_t vh = smem_base + OFF_RING + s * HALF + wt0 * 64 + t2 * 64 + c * 4;
                 const uint32_t pb = smem_base + OFF_P + warp * TW * 32 + t2 * 32;
+                const uint32_t xyl = smem_base + OFF_XY + (c & (XY_COPIES - 1)) * 8;
                 #pragma unroll 4
                 for (int st = 0; st < TW / 2; ++st) {
                     const uint32_t w = lds_u32(vh + st * 128);
@@ -360,13 +381,9 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
                     lds_f2x2(pb + st * 64 + 16, pp[2], pp[3]);
                     const f32x2 zz = f2_add(f2_pack(__int_as_float(__byte_perm(w, 0x4B000000u, 0x7514)),
                                                     __int_as_float(__byte_perm(w, 0x4B000000u, 0x7534))), negm);
-                    const float2 rr = f2_unpack(f2_add(f2_pack(__int_as_float((w & 0xF0u) | 0x4B000000u),
-                                                               __int_as_float(((w >> 16) & 0xF0u) | 0x4B000000u)),
-                                                       negm));
-                    const float2 csa = lds_f32x2(csb | ((w << 3) & 0x78u));      // table is 128-byte aligned
-                    const float2 csv = lds_f32x2(csb | ((w >> 13) & 0x78u));
-                    const f32x2 xa = f2_pack(rr.x * csa.x, rr.x * csa.y);
-                    const f32x2 xb = f2_pack(rr.y * csv.x, rr.y * csv.y);
+                    // (x, y) of both codes from the flat bytes 0 and 2: row e at e * 64, this lane's copy
+                    const f32x2 xa = lds_f2(xyl + __byte_perm(w, 0u, 0x4440) * 64u);
+                    const f32x2 xb = lds_f2(xyl + __byte_perm(w, 0u, 0x4442) * 64u);
                     #pragma unroll
                     for (int h = 0; h < HQ; ++h) {
                         azz[h] = f2_fma(pp[h], zz, azz[h]);
@@ -375,9 +392,9 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
                     }
                 }
             }
-            __syncwarp();
+            __syncwarp();                                   // pbuf is rewritten by the next tile
             if (lane == 0) mbar_arrive(&empty[s]);
-            ++seq;
+            if (++slot == SLOTS) { slot = 0; phase ^= 1u; }
         }
         {                                                  // prefetch the next item's queries
             WorkCursor pc = wc;
@@ -422,8 +439,8 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
             sWl[warp * HQ + 2 * lane + 1] = lsf.y;
         }
         named_bar_sync(1, nthr);
-        if (tid < HQ * 96) {
-            const int h = tid / 96, k = tid % 96;
+        for (int t = tid; t < HQ * 96; t += nthr) {
+            const int h = t / 96, k = t % 96;
             float M = -INFINITY;
             #pragma unroll
             for (int w = 0; w < W; ++w) M = fmaxf(M, sWm[w * HQ + h]);

@@ -36,24 +36,25 @@ constexpr int kNoallocMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocBytes];
 
 static std::mutex g_noalloc_mu;
-static void* g_noalloc_ptr[kNoallocMaxDevices] = {};
+static void* g_noalloc_zeroed[kNoallocMaxDevices] = {};
 
-// Address of this device's copy of the scratch array; resolved (and its
-// counter region zeroed on `st`) by the first call made with the device current.
+// Address of the current context's copy of the scratch array, looked up on every call (cheap;
+// a device reset or another context on the device gives another address).  The first call that
+// sees an address on a device zeroes its counter region on `st`.
 static int noalloc_scratch(cudaStream_t st, unsigned char** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) return PKV_ERR_CUDA;
     if (dev < 0 || dev >= kNoallocMaxDevices) return PKV_ERR_UNSUPPORTED;
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return PKV_ERR_CUDA;
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-        void* ptr = nullptr;
-        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return PKV_ERR_CUDA;
+    if (g_noalloc_zeroed[dev] != ptr) {
         if (cudaMemsetAsync(static_cast<unsigned char*>(ptr) + kCountOff, 0, kNoallocBytes - kCountOff, st) !=
             cudaSuccess)
             return PKV_ERR_CUDA;
-        g_noalloc_ptr[dev] = ptr;
+        g_noalloc_zeroed[dev] = ptr;
     }
-    *out = static_cast<unsigned char*>(g_noalloc_ptr[dev]);
+    *out = static_cast<unsigned char*>(ptr);
     return PKV_OK;
 }
 

@@ -70,8 +70,8 @@ class _DeviceArray:
 class SequenceExchange:
     """The split-sequence exchange of pkv_attn_decode_xr: one buffer per rank, merged in-kernel.
 
-    Every rank allocates one zeroed device buffer (pkv_xr_alloc: cudaMalloc, no multicast
-    object) and exports its CUDA IPC handle; the handles are all-gathered over the process group
+    Every rank allocates one zeroed device buffer (pkv_xr_alloc: plain cudaMalloc memory, not
+    bound to any NVSwitch object) and exports its CUDA IPC handle; the handles are all-gathered over the process group
     and every rank maps every peer's buffer (pkv_xr_open, plain peer memory over NVLink).  A
     decode step is then ONE kernel launch per rank: the kernel stores each finished unit's
     partial rows into every rank's buffer, counts its arrival at the unit's owner rank, and the

@@ -8,7 +8,8 @@ npz format (same keys, so files move between the two implementations).
 The encode hot path does not call ``encode_xy``: ``pkv_encode`` searches the
 table of bin ``i_z`` inside the fused encode kernel.  ``encode_xy`` /
 ``decode_xy`` are kept as tensor helpers on whatever device the inputs are.
-``train`` is offline calibration (k-means per z-bin).
+Training a codebook (the reference's offline k-means) is not part of this
+path: tables are trained once, saved, and loaded here.
 """
 
 from __future__ import annotations
@@ -18,34 +19,6 @@ from typing import Optional, Tuple
 
 import numpy as np
 import torch
-
-
-def _kmeans(pts: torch.Tensor, K: int, max_iter: int = 100, tol: float = 1e-4, seed: int = 0) -> torch.Tensor:
-    """Lloyd's k-means on 2-D points (random-subset init, empty clusters re-seeded)."""
-    dev = pts.device
-    if pts.shape[0] == 0:
-        return torch.zeros(K, 2, device=dev)
-    gen = torch.Generator(device=dev).manual_seed(seed)
-    pts = pts.float()
-    if pts.shape[0] < K:
-        reps = K // pts.shape[0] + 1
-        pts = pts.repeat(reps, 1)[:K] + torch.randn(K, 2, generator=gen, device=dev) * 1e-6
-    cent = pts[torch.randperm(pts.shape[0], generator=gen, device=dev)[:K]].clone()
-    for _ in range(max_iter):
-        assign = torch.cdist(pts, cent).argmin(dim=1)
-        sums = torch.zeros_like(cent).index_add_(0, assign, pts)
-        counts = torch.bincount(assign, minlength=K).to(pts.dtype)
-        new = torch.where(counts[:, None] > 0, sums / counts.clamp_min(1)[:, None], cent)
-        empty = counts == 0
-        if empty.any():
-            n = int(empty.sum())
-            pick = torch.randperm(pts.shape[0], generator=gen, device=dev)[:n]
-            new[empty] = pts[pick] + torch.randn(n, 2, generator=gen, device=dev) * 1e-4
-        shift = (new - cent).norm().item()
-        cent = new
-        if shift < tol:
-            break
-    return cent
 
 
 class LearnedSliceCodebook:
@@ -61,20 +34,6 @@ class LearnedSliceCodebook:
         self.z_min = z_min
         self.z_max = z_max
         self.r_max = r_max
-
-    @classmethod
-    def train(cls, rotated_vectors: torch.Tensor, z_idx: torch.Tensor, x_idx: torch.Tensor,
-              y_idx: torch.Tensor, z_min: float, z_max: float, r_max: float, bins_z: int, K: int,
-              max_iter: int = 100, tol: float = 1e-4, seed: int = 0) -> "LearnedSliceCodebook":
-        """Fit K centroids per uniform z-bin on all triplets of ``rotated_vectors`` (offline)."""
-        z = rotated_vectors[:, z_idx].float()
-        xy = torch.stack([rotated_vectors[:, x_idx].float(), rotated_vectors[:, y_idx].float()], -1).reshape(-1, 2)
-        dz = (z_max - z_min) / bins_z
-        iz = ((z - z_min) / dz).floor().long().clamp(0, bins_z - 1).reshape(-1)
-        cbs = torch.zeros(bins_z, K, 2)
-        for b in range(bins_z):
-            cbs[b] = _kmeans(xy[iz == b], K, max_iter=max_iter, tol=tol, seed=seed + b).cpu()
-        return cls(cbs, bins_z=bins_z, K=K, z_min=z_min, z_max=z_max, r_max=r_max)
 
     def encode_xy(self, xy: torch.Tensor, i_z: torch.Tensor) -> torch.Tensor:
         """(N, m, 2) points, (N, m) bins -> index of the nearest centroid of each point's bin."""
@@ -110,5 +69,5 @@ class LearnedSliceCodebook:
         return torch.sqrt(self.codebooks[..., 0] ** 2 + self.codebooks[..., 1] ** 2)
 
     def __repr__(self) -> str:
-        return (f"LearnedSliceCodebook(bins_z={self.bins_z}, K={self.K}, "
-                f"z=[{self.z_min:.2f}, {self.z_max:.2f}], r_max={self.r_max:.2f})")
+        return (f"<LearnedSliceCodebook {self.bins_z} z-bins x {self.K} centroids, "
+                f"z in [{self.z_min:.2f}, {self.z_max:.2f}], r <= {self.r_max:.2f}>")

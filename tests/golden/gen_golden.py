@@ -1,9 +1,10 @@
 """Generate golden vectors by running the PrismKV reference implementation.
 
-Run in a container where the reference is mounted (it is not needed, and
-not present, where the tests run):
+Run with the reference's ``src/`` directory on ``PYTHONPATH`` (the reference
+is needed only to regenerate the fixtures; the tests read the committed
+files):
 
-    PYTHONPATH=/root/reference/src python tests/golden/gen_golden.py
+    PYTHONPATH=<PrismKV checkout>/src python tests/golden/gen_golden.py
 
 Each case runs the reference's own public API on seeded inputs and stores
 inputs and outputs in ``tests/golden/<case>.npz``.  The rotation ``R`` is
@@ -240,7 +241,31 @@ def vllm_block_case(ref):
          k_dec=kd.numpy(), v_dec=vd.numpy(), **quant_state(comp._backends[1]._quantizer))
 
 
-CASES = {"enc": None, "backend_d64": backend_case, "attn_v1": attn_v1_case, "attn_v2_gqa": attn_v2_gqa_case,
+def files_case(ref):
+    """The reference writes a prismkv-cb-v1 codebook file and a Lloyd-Max z file with its own save
+    methods (learned_codebook.py:275-323, lloyd_max.py:156-185), then encodes seeded vectors after
+    loading each file into a fresh quantizer (stacked_plane.py:183-204, :349-356)."""
+    g = torch.Generator().manual_seed(21)
+    q = ref["SPQ"](dim=96, bits_z=4, bits_r=4, bits_theta=4, seed=42)
+    cb = ref["LSC"](synthetic_codebook(16, 256, q.r_max, 13), bins_z=16, K=256, z_min=q.z_min, z_max=q.z_max,
+                    r_max=q.r_max)
+    cb_path = os.path.join(HERE, "ref_codebook_444.npz")
+    cb.save(cb_path)
+    lq = ref["SPQ"](dim=96, bits_z=4, bits_r=4, bits_theta=4, seed=42)
+    lq.calibrate_lloyd_max_z(torch.randn(4096, 96, generator=g))
+    lm_path = os.path.join(HERE, "ref_lloyd_z.npz")
+    lq.save_lloyd_max_z(lm_path)
+    x = torch.cat([torch.randn(512, 96, generator=g) * 1.3, edge_rows(q.R, g)])
+    qc = ref["SPQ"](dim=96, bits_z=4, bits_r=4, bits_theta=4, seed=42)
+    qc.load_codebooks(cb_path)
+    ql = ref["SPQ"](dim=96, bits_z=4, bits_r=4, bits_theta=4, seed=42)
+    ql.load_lloyd_max_z(lm_path)
+    save("files_codes", x=x.numpy(), codes_cb=qc.encode(x).numpy().astype(np.int16),
+         codes_lloyd=ql.encode(x).numpy().astype(np.int16),
+         R=q.R.numpy().astype(np.float32))
+
+
+CASES = {"files": files_case, "enc": None, "backend_d64": backend_case, "attn_v1": attn_v1_case, "attn_v2_gqa": attn_v2_gqa_case,
          "raw_cache_d64": raw_cache_case, "kv_cache_d96": kv_cache_case, "vllm_block_d64": vllm_block_case}
 
 
@@ -269,6 +294,7 @@ def main():
     raw_cache_case(ref)
     kv_cache_case(ref)
     vllm_block_case(ref)
+    files_case(ref)
 
 
 if __name__ == "__main__":

@@ -15,7 +15,7 @@ def test_config_matches_reference_formulas():
     assert (c.bits_z, c.bits_r, c.bits_theta, c.rotation_seed, c.codebook_path) == (4, 4, 4, 42, None)
     assert c.bits_per_dim == 4.0 and c.compression_vs_fp16 == 4.0
     c2 = PrismKVConfig(3, 3, 2)
-    assert c2.bits_per_dim == pytest.approx(8 / 3) and "2.7 bits/dim" in repr(c2)
+    assert c2.bits_per_dim == pytest.approx(8 / 3) and "2.67 bits/dim" in repr(c2)
 
 
 @pytest.mark.parametrize("d,padded", [(64, 66), (96, 96), (128, 129), (65, 66)])

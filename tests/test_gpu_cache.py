@@ -153,3 +153,25 @@ def test_vllm_block_codec_matches_reference(cuda_ready):
     comp.evict_block(1, 7)
     with pytest.raises(KeyError):
         comp.decompress_block(1, 7, 2, 16)
+
+
+def test_vllm_swap_loop_reuses_pinned_buffers(cuda_ready):
+    """A swap loop without a per-block host wait: blocks compressed with sync=False decompress
+    correctly (stream order), synchronize() makes their host codes complete, and an evicted
+    block's pinned buffers serve the next block of the same shape."""
+    comp = VLLMSwapCompressor(PrismKVConfig(), head_dim=96, n_layers=1)
+    g = torch.Generator(device=DEV).manual_seed(3)
+    blocks = [(torch.randn(4, 16, 96, generator=g, device=DEV).half(),
+               torch.randn(4, 16, 96, generator=g, device=DEV).half()) for _ in range(3)]
+    kept = [comp.compress_block(0, i, kb, vb, sync=False) for i, (kb, vb) in enumerate(blocks)]
+    for i, (kb, vb) in enumerate(blocks):
+        kd, vd = comp.decompress_block(0, i, 4, 16, dtype=torch.float32, device=DEV)
+        ref_k = comp._backends[0].codec(torch.device(DEV)).decode(
+            comp._backends[0].codec(torch.device(DEV)).encode(kb.reshape(64, 96), code_dtype=torch.int16))
+        np.testing.assert_allclose(kd.reshape(64, 96).cpu().numpy(), ref_k.cpu().numpy(), atol=1e-6)
+    comp.synchronize()
+    first_k = kept[0][0]
+    comp.evict_block(0, 0)
+    kc, _ = comp.compress_block(0, 9, *blocks[1])
+    assert kc.data_ptr() == first_k.data_ptr() or kept[0][1].data_ptr() == kc.data_ptr()
+    assert comp.n_compressed_blocks == 3

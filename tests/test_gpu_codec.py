@@ -285,3 +285,27 @@ def test_tensor_core_encode_edge_rows(cuda_ready):
         with _force_cuda_core(codec):
             cc = codec.encode(X)
         assert torch.equal(tc, cc), variant
+
+
+@pytest.mark.parametrize("which", ["cb", "lloyd"])
+def test_encode_after_loading_reference_written_files(cuda_ready, which):
+    """A codebook / Lloyd-Max file written by the reference, loaded through the drop-in API, gives
+    the reference's codes on the GPU (rounding ties excepted, each proven in fp64)."""
+    import os
+    from conftest import GOLDEN
+    from prismkv_b200 import StackedPlaneQuantizer
+    f = load_golden("files_codes")
+    q = StackedPlaneQuantizer(96, 4, 4, 4, seed=42)
+    p = oracle.QuantParams.default(96)
+    if which == "cb":
+        q.load_codebooks(os.path.join(GOLDEN, "ref_codebook_444.npz"))
+        p.codebook = q._codebooks.codebooks.numpy()
+        p.z_min, p.z_max, p.r_max = q.z_min, q.z_max, q.r_max
+    else:
+        q.load_lloyd_max_z(os.path.join(GOLDEN, "ref_lloyd_z.npz"))
+        p.lloyd_boundaries = q._lloyd_max_z.boundaries.numpy()
+        p.lloyd_centroids = q._lloyd_max_z.centroids.numpy()
+    codes = q.encode(torch.from_numpy(f["x"]).to(DEV)).cpu().numpy()
+    rep = oracle.classify(f["x"], f["R"], p, codes, f[f"codes_{which}"].astype(np.int64) & 0xFFF)
+    assert rep.unexplained == 0, rep.examples
+    assert rep.mismatches <= max(2, int(rep.total * TIE_RATE))

@@ -7,8 +7,10 @@ entry point on the same inputs.  Tolerance 1e-6 absolute: both run the same
 kernel and merge, so any difference beyond float noise is a scratch bug.
 Each case calls the no-alloc entry point twice in a row, which checks that a
 call leaves the arrival counters at zero for the next one.  This file is
-named to be collected last, so it runs both after the other GPU tests and
-alone in a fresh process.
+named to be collected last, so that a full run reaches it after every other
+GPU test; it passes on its own too (``pytest tests/test_zz_no_alloc.py`` in a
+fresh process), where its first call is the library's first touch of the
+scratch array.
 """
 
 import ctypes
