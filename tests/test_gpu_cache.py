@@ -175,3 +175,47 @@ def test_vllm_swap_loop_reuses_pinned_buffers(cuda_ready):
     kc, _ = comp.compress_block(0, 9, *blocks[1])
     assert kc.data_ptr() == first_k.data_ptr() or kept[0][1].data_ptr() == kc.data_ptr()
     assert comp.n_compressed_blocks == 3
+
+
+def test_sidecar_json_and_binary_agree_with_the_reference(cuda_ready):
+    """The sidecar's JSON API gives the reference backend's codes (golden backend_d64, through
+    PrismKVBackend.compress); the binary transport gives the same codes and the same decoded
+    vectors with raw arrays instead of decimal lists."""
+    import json as _json
+    import urllib.request
+    from prismkv_b200 import sidecar
+    f = load_golden("backend_d64")
+    k, v = f["k"].astype(np.float32), f["v"].astype(np.float32)
+    srv = sidecar.PrismKVSidecar(port=0)
+    srv.start_background()
+    url = f"http://127.0.0.1:{srv.port}"
+    try:
+        req = urllib.request.Request(url + "/compress", method="POST", headers={"Content-Type": "application/json"},
+                                     data=_json.dumps({"k": k.tolist(), "v": v.tolist()}).encode())
+        with urllib.request.urlopen(req, timeout=60) as r:
+            js = _json.loads(r.read())
+        kc_json = np.array(js["k_codes"], dtype=np.int16)
+        assert js["n_groups"] == 22 and js["head_dim"] == 64
+        _codes_match(f, _pad(k, 66), kc_json, f["k_codes"])
+        req = urllib.request.Request(url + "/compress", method="POST", data=k.tobytes() + v.tobytes(),
+                                     headers={"Content-Type": sidecar.BINARY, "X-PrismKV-Shape": f"{k.shape[0]},64"})
+        with urllib.request.urlopen(req, timeout=60) as r:
+            raw = r.read()
+            assert r.headers["X-PrismKV-Shape"] == f"{k.shape[0]},22"
+        codes = np.frombuffer(raw, dtype=np.int16).reshape(2, k.shape[0], 22)
+        np.testing.assert_array_equal(codes[0], kc_json)
+        np.testing.assert_array_equal(codes[1], np.array(js["v_codes"], dtype=np.int16))
+        req = urllib.request.Request(url + "/decompress", method="POST", data=raw,
+                                     headers={"Content-Type": sidecar.BINARY, "X-PrismKV-Shape": f"{k.shape[0]},22",
+                                              "X-PrismKV-Head-Dim": "64"})
+        with urllib.request.urlopen(req, timeout=60) as r:
+            dec = np.frombuffer(r.read(), dtype=np.float32).reshape(2, k.shape[0], 64)
+        req = urllib.request.Request(url + "/decompress", method="POST", headers={"Content-Type": "application/json"},
+                                     data=_json.dumps({"k_codes": js["k_codes"], "v_codes": js["v_codes"],
+                                                       "head_dim": 64}).encode())
+        with urllib.request.urlopen(req, timeout=60) as r:
+            jd = _json.loads(r.read())
+        np.testing.assert_array_equal(dec[0], np.array(jd["k"], dtype=np.float32))
+        np.testing.assert_array_equal(dec[1], np.array(jd["v"], dtype=np.float32))
+    finally:
+        srv.stop()
