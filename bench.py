@@ -455,18 +455,18 @@ def bench_decode(args, ws, rank, device):
         torch.cuda.synchronize(device)
         attn_only_ms = sum(a_.elapsed_time(b_) for a_, b_ in ks) / len(ks)
         _barrier(ws)
-        if exchange is None:
-            # the all-gather path's launches captured in one CUDA graph, so the host's launch gaps
-            # between them leave the timed step (the exchange path is one launch already)
-            g_ = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g_):
-                seq_step()
-            graphs.append(g_)
-            torch.cuda.synchronize(device)
-            _barrier(ws)
-            for j in range(4):
-                scrub()
-                graphs[0].replay()
+        # the step's launches captured in one CUDA graph (the all-gather path: attention, NCCL,
+        # combine; the exchange path: its one kernel), so host-side Python between the timing
+        # events and the launch stays out of the timed step
+        g_ = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_):
+            seq_step()
+        graphs.append(g_)
+        torch.cuda.synchronize(device)
+        _barrier(ws)
+        for j in range(4):
+            scrub()
+            graphs[0].replay()
     torch.cuda.synchronize(device)
     _barrier(ws)
     torch.cuda.synchronize(device)
@@ -561,7 +561,7 @@ def bench_decode(args, ws, rank, device):
         line["attn_ms_per_step"] = round(local_kern_ms, 5)
         line["config"]["step"] = ("one kernel per rank: attention over the shard, partials stored into every "
                                   "rank's buffer, merge + R by the rank completing each unit's count, bounded "
-                                  "completion wait" if exchange is not None else
+                                  "completion wait; replayed from a CUDA graph" if exchange is not None else
                                   "partial attention + NCCL all-gather + LSE combine, one CUDA graph per step")
     graphs.clear()                              # release the graphs holding collectives before teardown
     if exchange is not None:

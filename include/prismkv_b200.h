@@ -61,6 +61,8 @@ enum {
 
 /* ---- codec flags -------------------------------------------------------- */
 #define PKV_CODEC_Z_UNIFORM 1   /* uniform z bins without BiasTable (dec_z affine in i_z) */
+#define PKV_CODEC_FP32_ATTN 2   /* attention arithmetic in fp32 throughout: no fp16-pair
+                                   tensor-core tiles (attn_gqa12_mma_kernel is not planned) */
 
 /* ---- element types ----------------------------------------------------- */
 enum { PKV_F32 = 0, PKV_BF16 = 1, PKV_F16 = 2 };
@@ -188,7 +190,7 @@ PKV_API int pkv_attn_decode(const pkv_codec *c, const pkv_attn_args *a,
  * (introspection for tests and benchmarks; launches nothing; the output
  * pointers of `a` may be null).                                           */
 enum { PKV_KERNEL_MHA12 = 1, PKV_KERNEL_POLAR = 2, PKV_KERNEL_LUT = 3, PKV_KERNEL_TC = 4, PKV_KERNEL_MHA8 = 5,
-       PKV_KERNEL_MHA12_STREAM = 6, PKV_KERNEL_GQA12 = 7 };
+       PKV_KERNEL_MHA12_STREAM = 6, PKV_KERNEL_GQA12 = 7, PKV_KERNEL_GQA12_MMA = 8 };
 typedef struct pkv_attn_plan {
     int32_t kernel;            /* PKV_KERNEL_*                                  */
     int32_t num_splits;        /* sequence splits per (batch, kv head)          */

@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(HERE, "libprismkv_b200.so")
 PKV_OK = 0
 PKV_F32, PKV_BF16, PKV_F16 = 0, 1, 2
 PKV_CODEC_Z_UNIFORM = 1
+PKV_CODEC_FP32_ATTN = 2
 DTYPE_CODES = {torch.float32: PKV_F32, torch.bfloat16: PKV_BF16, torch.float16: PKV_F16}
 
 EXPORTED = ("pkv_abi_version", "pkv_strerror", "pkv_device_error", "pkv_encode", "pkv_decode",
@@ -65,7 +66,8 @@ class PkvXrLayout(ctypes.Structure):
 
 
 KERNEL_NAMES = {1: "attn_mha12_kernel", 2: "attn_polar_kernel", 3: "attn_lut_kernel", 4: "attn_tc_kernel",
-                5: "attn_mha8_kernel", 6: "attn_mha12_stream_kernel", 7: "attn_gqa12_kernel"}
+                5: "attn_mha8_kernel", 6: "attn_mha12_stream_kernel", 7: "attn_gqa12_kernel",
+                8: "attn_gqa12_mma_kernel"}
 
 _lock = threading.Lock()
 _lib = None

@@ -107,6 +107,19 @@ class DeviceCodec:
         self._ws: Dict[int, torch.Tensor] = {}
         self.R = self._R.view(host.dim, host.dim)
 
+    @property
+    def fp32_attention(self) -> bool:
+        """Attention arithmetic in fp32 throughout: the grouped 12-bit decode then runs on the fp32
+        kernel instead of the fp16-pair tensor-core one (both are within 1e-5 of fp64)."""
+        return bool(self.struct.flags & _lib.PKV_CODEC_FP32_ATTN)
+
+    @fp32_attention.setter
+    def fp32_attention(self, on: bool) -> None:
+        if on:
+            self.struct.flags |= _lib.PKV_CODEC_FP32_ATTN
+        else:
+            self.struct.flags &= ~_lib.PKV_CODEC_FP32_ATTN
+
     # ------------------------------------------------------------------
     def _stream(self) -> int:
         return _lib.stream_ptr(self.device)

@@ -244,6 +244,8 @@ __device__ __forceinline__ void red_add_release_sys(uint32_t* ptr, uint32_t v) {
     asm volatile("red.add.release.sys.global.u32 [%0], %1;" :: "l"(ptr), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
@@ -332,9 +334,11 @@ __device__ void rotate_out(const AttnParams& p, const ItemRange& r, float* sO, c
 __device__ void xr_arrive(const AttnParams& p, const ItemRange& r, float* sO, float* sFin, int* sflag,
                           const float* Rp, int pitch, int tid, int nthr, int max_parts) {
     const int dim = p.dim, greal = p.G;
-    __threadfence_system();
+    // the CTA's peer stores are ordered before thread 0's system-scope release by the barrier
+    // (causality is transitive through bar.sync): one fence for the CTA, not one per thread
     named_bar_sync(1, nthr);
     if (tid == 0) {
+        fence_acq_rel_sys();
         const int unit = r.b * p.Hu + r.hk;
         uint32_t* cnt = reinterpret_cast<uint32_t*>(p.xr_buf[unit % p.xr_world] + p.xr_cnt_off) + unit;
         const uint32_t old = atom_add_acq_rel_sys(cnt, 1u);
@@ -361,11 +365,12 @@ __device__ void xr_arrive(const AttnParams& p, const ItemRange& r, float* sO, fl
         sFin[g * dim + k] = (l > 0.f) ? v / l : 0.f;
     }
     rotate_out(p, r, sO, sFin, Rp, pitch, tid, nthr, max_parts);
-    __threadfence_system();
     named_bar_sync(1, nthr);
-    if (tid == 0)
+    if (tid == 0) {
+        fence_acq_rel_sys();
         for (int s = 0; s < p.xr_world; ++s)
             red_add_release_sys(reinterpret_cast<uint32_t*>(p.xr_buf[s] + p.xr_done_off), 1u);
+    }
 }
 
 // Exchange mode, once per CTA after its last item: the rank's last CTA waits until every unit's
@@ -1154,6 +1159,7 @@ static int round_group(int G) { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
 #include "pkv_attn_mha8.cu"
 #include "pkv_attn_mha12.cu"
 #include "pkv_attn_gqa12.cu"
+#include "pkv_attn_gqa12m.cu"
 
 namespace pkv {
 
@@ -1162,6 +1168,7 @@ struct AttnPlan {
     bool mha12s;
     bool mha8;                         // attn_mha8_kernel
     bool gqa12;                        // attn_gqa12_kernel: four query heads of one KV head per unit
+    bool g12m;                         // ... as attn_gqa12_mma_kernel (fp16-pair tensor-core tiles)
     bool polar;                        // attn_polar_kernel, else attn_lut_kernel
     int G, TPL, stages, nsplit, chunk, tt, threads, smem, ctas_per_sm;
     bool tma;
@@ -1204,6 +1211,8 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
     if (pl.gqa12) {
         pl.mha12 = false;
         pl.qunits = false;
+        // the tensor-core form holds the decoded (x, y) as fp16 pairs: radii up to 2^15
+        pl.g12m = (c->flags & PKV_CODEC_FP32_ATTN) == 0 && c->r_max > 0.f && c->r_max <= 32768.f;
     }
     if (pl.mha12) {
         pl.G = 1;
@@ -1232,10 +1241,10 @@ static AttnPlan plan_attn(const pkv_codec* c, const pkv_attn_args* a) {
         pl.polar = false;
         pl.TPL = 1;
         pl.G = gqa12::HQ;
-        pl.tt = gqa12::TT;
-        pl.threads = gqa12::W * 32 + 32;
-        pl.stages = gqa12::SLOTS;
-        pl.smem = gqa12::TOTAL;
+        pl.tt = pl.g12m ? g12m::TT : gqa12::TT;
+        pl.threads = pl.g12m ? g12m::W * 32 + 32 : gqa12::W * 32 + 32;
+        pl.stages = pl.g12m ? g12m::SLOTS : gqa12::SLOTS;
+        pl.smem = pl.g12m ? g12m::TOTAL : gqa12::TOTAL;
         pl.chunk = 1 << 30;                // online softmax: no cap on the tokens of an item
         pl.ctas_per_sm = 1;
     } else if (pl.tc) {
@@ -1366,7 +1375,7 @@ bool attn_group_supported(const pkv_codec* c, const pkv_attn_args* a) {
 void describe_attn(const pkv_codec* c, const pkv_attn_args* a, pkv_attn_plan* out) {
     const AttnPlan pl = plan_attn(c, a);
     out->kernel = pl.tc      ? PKV_KERNEL_TC
-                  : pl.gqa12 ? PKV_KERNEL_GQA12
+                  : pl.gqa12 ? (pl.g12m ? PKV_KERNEL_GQA12_MMA : PKV_KERNEL_GQA12)
                   : pl.mha12 ? (pl.mha12s ? PKV_KERNEL_MHA12_STREAM : PKV_KERNEL_MHA12)
                   : pl.mha8  ? PKV_KERNEL_MHA8
                              : (pl.polar ? PKV_KERNEL_POLAR : PKV_KERNEL_LUT);
@@ -1539,7 +1548,8 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
                          : pl.G == 8 ? launch_kernel(attn_tc_kernel<2, 8>, p, pl, st)
                                      : launch_kernel(attn_tc_kernel<2, 16>, p, pl, st);
     }
-    if (pl.gqa12) return launch_kernel(attn_gqa12_kernel, p, pl, st);
+    if (pl.gqa12) return pl.g12m ? launch_kernel(attn_gqa12_mma_kernel, p, pl, st)
+                                 : launch_kernel(attn_gqa12_kernel, p, pl, st);
     if (pl.mha12s) return launch_kernel(attn_mha12_stream_kernel, p, pl, st);
     if (pl.mha12) return launch_kernel(attn_mha12_kernel, p, pl, st);
     if (pl.mha8) return launch_kernel(attn_mha8_kernel, p, pl, st);

@@ -52,11 +52,14 @@ constexpr int OFF_P = OFF_QRAW + HQ * 96 * 4;           // [W][TW tokens][2] flo
 constexpr int OFF_WML = OFF_P + W * TW * 2 * 16;        // [W][4] max, [W][4] sum
 constexpr int OFF_FIN = OFF_WML + 2 * W * HQ * 4;       // [4][96]
 constexpr int OFF_MISC = OFF_FIN + HQ * 96 * 4;         // sM[4], sL[4], sC[4], flag
-constexpr int OFF_BAR = OFF_MISC + 64;                  // full[SLOTS], empty[SLOTS]
-constexpr int TOTAL = OFF_BAR + 2 * SLOTS * 8;
+constexpr int OFF_BAR = OFF_MISC + 64;                  // full[SLOTS], empty[SLOTS], rbar
+constexpr int TOTAL = OFF_BAR + (2 * SLOTS + 1) * 8;
 constexpr int OFF_ACC = OFF_KT;                         // item merge [W][4][96] over the dead table
+constexpr int OFF_R = OFF_KT + 32768;                   // R (fp32, row pitch 96) over the dead table
+constexpr int RBYTES = 96 * 96 * 4;
 constexpr float MAGIC = 8388608.f;                      // 2^23
-static_assert(W * HQ * 96 * 4 <= KT_BYTES, "merge buffer fits the table region");
+static_assert(W * HQ * 96 * 4 <= OFF_R - OFF_KT && OFF_R + RBYTES <= OFF_KT + KT_BYTES,
+              "merge buffer and R fit the table region side by side");
 static_assert(OFF_RING % 128 == 0 && OFF_XY % 128 == 0 && OFF_CS % 128 == 0 && OFF_P % 16 == 0 &&
               OFF_BAR % 8 == 0, "alignment");
 static_assert(TOTAL <= 227 * 1024, "one CTA per SM");
@@ -127,10 +130,10 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
     int* sflag = reinterpret_cast<int*>(sM + 12);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + SLOTS;
+    uint64_t* rbar = empty + SLOTS;
+    const float* sR = reinterpret_cast<const float*>(smem + OFF_R);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int R_LINES = 96 * 96 * 4 / 128;           // R is read from L2 by every item
-    for (int i = tid; i < R_LINES; i += blockDim.x) prefetch_l2(p.R + i * 32);
     const float dr = p.r_max / 15.f;
     const float z0 = __ldg(p.dec_z), dz = __ldg(p.dec_z + 1) - z0;      // uniform z bins: z = z0 + i dz
 
@@ -144,7 +147,12 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], W);
         }
+        mbar_init(rbar, 1);
         fence_mbar_init();
+        // R for the first item's query rotation; the table overwrites it, and every item's end
+        // brings it back for the finish and the next rotation
+        mbar_arrive_expect_tx(rbar, RBYTES);
+        bulk_g2s(smem + OFF_R, p.R, RBYTES, rbar);
     }
     // V's (x, y) table: row e = (i_r << 4) | i_theta holds XY_COPIES copies of (16 i_r) * vCS[i_theta]
     // (the same product as the radius times the (cos, sin) table), copy k at bytes 8k of the row:
@@ -184,7 +192,10 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
     float4* pbuf = reinterpret_cast<float4*>(smem + OFF_P) + warp * TW * 2;
     int slot = 0;                                        // ring slot of the next half tile, its fill phase
     uint32_t phase = 0;
+    uint32_t rphase = 0;                                 // phase of the next R copy
     bool alive = true;
+    if (!mbar_wait(rbar, rphase, kErrWaitFull)) alive = false;
+    rphase ^= 1u;
     WorkCursor wc = work_begin(p);
     ItemRange r;
     while (work_next<true>(p, wc, r)) {
@@ -197,8 +208,8 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
         // one of the pair), then a butterfly over the low three lane bits
         #pragma unroll 1
         for (int k = warp; k < 96; k += W) {
-            const float* row = p.R + k * 96;
-            const float r0 = __ldg(row + lane), r1 = __ldg(row + lane + 32), r2 = __ldg(row + lane + 64);
+            const float* row = sR + k * 96;
+            const float r0 = row[lane], r1 = row[lane + 32], r2 = row[lane + 64];
             float a[HQ];
             #pragma unroll
             for (int h = 0; h < HQ; ++h)
@@ -282,27 +293,25 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
                 #pragma unroll
                 for (int it = 0; it < 4; ++it) {
                     const uint2 cw = lds_u32x2(kslot + (kofs ^ (it << 8)));
-                    f32x2 T01[4], T23[4], zz[4];
+                    f32x2 s01, s23;
                     #pragma unroll
                     for (int u = 0; u < 2; ++u) {
                         const uint32_t w = u ? cw.y : cw.x;
                         // flat * 256 + 16 g from one byte permute (byte 0 from the lane's slot)
                         const uint32_t ea = __byte_perm(w, kt_g, 0x5504), eb = __byte_perm(w, kt_g, 0x5524);
-                        lds_f2x2(ktab + u * KT_HALF + ea, T01[2 * u], T23[2 * u]);
-                        lds_f2x2(ktab + u * KT_HALF + 128 + eb, T01[2 * u + 1], T23[2 * u + 1]);
+                        f32x2 ta01, ta23, tb01, tb23;
+                        lds_f2x2(ktab + u * KT_HALF + ea, ta01, ta23);
+                        lds_f2x2(ktab + u * KT_HALF + 128 + eb, tb01, tb23);
                         // (0.5 + i_z / 256) twice, from the byte holding i_z (two selectors that
                         // pick the same bytes, so that the pair is two independent permutes)
-                        zz[2 * u] = f2_pack(__int_as_float(__byte_perm(w, 0x3F000000u, 0x7144)),
-                                            __int_as_float(__byte_perm(w, 0x3F000000u, 0x7155)));
-                        zz[2 * u + 1] = f2_pack(__int_as_float(__byte_perm(w, 0x3F000000u, 0x7344)),
-                                                __int_as_float(__byte_perm(w, 0x3F000000u, 0x7355)));
-                    }
-                    f32x2 s01 = f2_add(f2_add(T01[0], T01[1]), f2_add(T01[2], T01[3]));
-                    f32x2 s23 = f2_add(f2_add(T23[0], T23[1]), f2_add(T23[2], T23[3]));
-                    #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        s01 = f2_fma(az01[i], zz[i], s01);
-                        s23 = f2_fma(az23[i], zz[i], s23);
+                        const f32x2 za = f2_pack(__int_as_float(__byte_perm(w, 0x3F000000u, 0x7144)),
+                                                 __int_as_float(__byte_perm(w, 0x3F000000u, 0x7155)));
+                        const f32x2 zb = f2_pack(__int_as_float(__byte_perm(w, 0x3F000000u, 0x7344)),
+                                                 __int_as_float(__byte_perm(w, 0x3F000000u, 0x7355)));
+                        const f32x2 t01 = f2_fma(az01[2 * u + 1], zb, f2_fma(az01[2 * u], za, f2_add(ta01, tb01)));
+                        const f32x2 t23 = f2_fma(az23[2 * u + 1], zb, f2_fma(az23[2 * u], za, f2_add(ta23, tb23)));
+                        s01 = u ? f2_add(s01, t01) : t01;
+                        s23 = u ? f2_add(s23, t23) : t23;
                     }
                     v01[it] = s01;
                     v23[it] = s23;
@@ -424,6 +433,11 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
             vb[h].y += __shfl_xor_sync(0xffffffffu, vb[h].y, 16);
         }
         named_bar_sync(1, nthr);                           // every warp is past its last table read
+        if (tid == 0) {                                    // R over the dead table, beside the merge buffer
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(rbar, RBYTES);
+            bulk_g2s(smem + OFF_R, p.R, RBYTES, rbar);
+        }
         if (lane < 16) {
             float* o = sAcc + warp * HQ * 96 + 6 * c;      // triplets 2c, 2c + 1
             #pragma unroll
@@ -460,8 +474,10 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
                 sL[h] = L;
             }
         }
+        if (alive && !mbar_wait(rbar, rphase, kErrWaitFull)) alive = false;
+        rphase ^= 1u;
         named_bar_sync(1, nthr);
-        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, 96, tid, nthr, 1);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 1);
     }
     xr_kernel_tail(p, tid, nthr);
 }

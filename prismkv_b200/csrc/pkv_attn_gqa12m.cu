@@ -1,0 +1,548 @@
+// pkv_attn_gqa12m.cu -- decode attention for grouped query heads over 12-bit (4+4+4) uniform-polar
+// codes of head_dim 96, with both contractions (q . k over the 96 dims, p . v over the tokens) on
+// the tensor cores as register-operand mma.sync tiles.  One work unit is four query heads of one
+// KV head (as in attn_gqa12_kernel); each code is decoded once, straight into an operand fragment.
+//
+// Why register-operand tiles and not tcgen05: a unit's four heads are the narrow side of both
+// products (n = 8 columns here; tcgen05 wants M >= 64 and operands in shared or tensor memory),
+// and the operands are produced by a table decode in registers.  Staging the decoded tiles
+// through shared memory for tcgen05 costs more issue slots and shared bandwidth than the
+// products themselves (the attn_tc_kernel design), so here the decode feeds the tiles directly.
+//
+// Numerics: every operand is an fp16 pair (hi, lo) with hi + lo equal to the fp32 value to about
+// 2^-22, and the pair rides either along the contraction or across the eight output columns:
+//  * the decoded (x, y) of a code sit in a table as (x_hi, x_lo), (y_hi, y_lo); a fragment's
+//    k-pair (2c, 2c + 1) is one such pair, so the product sums x_hi b + x_lo b;
+//  * the queries (and the softmax weights) enter as eight columns: column h < 4 holds head h's hi
+//    part and column h + 4 its lo part; the two columns are added once (scores per tile, output
+//    rows per item).  All four cross products are thus kept; products and sums are fp32.
+//  * z enters through its integer bin index i_z (exact): uniform bins are affine in i_z (z = z0 +
+//    dz i_z), so q . z = z0 sum q_z + dz sum q_z i_z, with i_z as the fp16 subnormal i_z 2^-24 of
+//    one byte permute, and o_z = (z0 + 8 dz) l + dz sum p (i_z - 8), with i_z - 8 as an exact fp16.
+//    The centring matters: the tensor-core sums truncate, and an uncentred sum p i_z grows with
+//    every token while the result is a small difference of it and z0 l.
+//  * the queries are scaled by a power of two per item (their largest |value| lands in
+//    [2^13, 2^14)) and the scores scaled back in the exponent; the weights are 2^12 exp2(s - m),
+//    which keeps them normal in fp16 down to 2^-26 of the largest.
+// The result is within a few 1e-6 of the fp64 softmax(q . decode(K)^T * scale) . decode(V)
+// (polar_attention.py:277-309 with decoded values) for head_dim 96 data.
+//
+// Layout of a warp's 16 tokens of a tile (lane = 4 g + c):
+//  * scores: rows = tokens, k = dims.  Lane (g, c) decodes tokens rho(g), rho(g) + 8 with
+//    rho(g) = (g >> 1) + 4 (g & 1), triplets 8c .. 8c + 7 (one 16-byte load a token): k-step j
+//    < 8 is the (x, y) pair of triplet 8c + j, k-steps 8, 9 the z indices of triplets 8c + 4j'
+//    .. 8c + 4j' + 3.  The permutation of the dims is the same for the query fragments.
+//  * weights: the score tile (rows = tokens rho(.), columns = head parts) is turned into the
+//    p . v operand by two 8x8 transposes (movmatrix): lane (g, c) then holds column g of tokens
+//    (c, c + 4) and (c + 8, c + 12).
+//  * values: rows = dims, k = tokens.  For (x, y) the k-pairs are (token, hi/lo), so a step
+//    covers 8 tokens and the weight operand is (p, p); rows g / g + 8 are x / y of triplet 4g + m
+//    (m-tile m < 4).  For z the k-pairs are two tokens and rows g / g + 8 are the z of triplets
+//    4g + 2m', 4g + 2m' + 1 (m-tiles 4, 5).  Lane (g, c) reads tokens c, c + 4, c + 8, c + 12,
+//    triplets 4g .. 4g + 3 (one 8-byte load a token).
+// Table lookups: 256 rows (the flat index (i_r << 4) | i_theta) of 32 copies, copy l at bytes
+// 8 l of the row, so a warp's 32 loads always take the minimum two wavefronts; the table sits at
+// a 64 KB-aligned shared address, so one byte permute of the code word and a per-lane register
+// gives the whole address.
+//
+// Work, ring and exchange as in attn_gqa12_kernel: one CTA per SM (15 consumer warps, one TMA
+// producer warp: four warps per SM sub-partition leave 128 registers a thread), persistent over
+// balanced tile ranges, half tiles (K or V codes of 240 tokens, 15 KB) through a ring of six
+// slots (four below the table, two above), bounded mbarrier waits, splits merged by the last CTA
+// (finish_item).
+
+namespace pkv {
+namespace g12m {
+constexpr int W = 15;                                   // consumer warps (16 warps: 128 registers)
+constexpr int HQ = 4;                                   // query heads per unit
+constexpr int TW = 16;                                  // tokens per warp per tile
+constexpr int TT = W * TW;                              // tokens per tile
+constexpr int HALF = TT * 64;                           // K (or V) codes of a tile: 32 x uint16 / token
+constexpr int SLOTS = 6;                                // ring of half tiles
+constexpr int TAB_BYTES = 256 * 32 * 8;                 // [256 flat][32 copies] (x hi|lo, y hi|lo)
+// The dynamic shared window of a kernel without static shared memory starts at shared address
+// 0x400 on sm_100 (the first KB is reserved; checked at run time).  The table must start at a
+// 64 KB-aligned shared address, so it sits at window offset 0x10000 - 0x400; the four ring slots
+// and the queries fill the window below it, the rest (two more slots among it) lies above.
+constexpr uint32_t SMEM_BASE = 0x400;
+constexpr int OFF_TAB = (int)((0x10000u - (SMEM_BASE & 0xFFFFu)) & 0xFFFFu);
+constexpr int SLOTS_LO = 4;                             // ring slots below the table
+constexpr int OFF_RING_LO = 0;
+constexpr int OFF_Q = OFF_RING_LO + SLOTS_LO * HALF;    // [4][96] rotated, scaled queries
+constexpr int OFF_QRAW = OFF_Q + HQ * 96 * 4;           // [4][96] raw queries
+constexpr int OFF_R = OFF_TAB + TAB_BYTES;              // R, fp32, row pitch 96 (resident)
+constexpr int RBYTES = 96 * 96 * 4;
+constexpr int OFF_ACC = OFF_R + RBYTES;                 // item merge [W][4][96]
+constexpr int OFF_WML = OFF_ACC + W * HQ * 96 * 4;      // [W][4] max, [W][4] sum
+constexpr int OFF_FIN = OFF_WML + 2 * W * HQ * 4;       // [4][96]
+constexpr int OFF_MISC = OFF_FIN + HQ * 96 * 4;         // sM[4], sL[4], sC[4], flag, amax[W]
+constexpr int OFF_BAR = OFF_MISC + 128;                 // full[SLOTS], empty[SLOTS], rbar
+constexpr int OFF_RING_HI = (OFF_BAR + (2 * SLOTS + 1) * 8 + 127) / 128 * 128;
+constexpr int TOTAL = OFF_RING_HI + (SLOTS - SLOTS_LO) * HALF;
+static_assert(OFF_QRAW + HQ * 96 * 4 <= OFF_TAB, "slots and queries below the table");
+static_assert(OFF_R % 128 == 0 && OFF_ACC % 16 == 0 && OFF_BAR % 8 == 0 && HALF % 128 == 0, "alignment");
+static_assert(TOTAL <= 227 * 1024, "one CTA per SM");
+static_assert(W * 32 >= HQ * 96, "one consumer thread per query element (the query prefetch)");
+
+// window offset of ring slot s
+__host__ __device__ constexpr int ring_off(int s) {
+    return s < SLOTS_LO ? OFF_RING_LO + s * HALF : OFF_RING_HI + (s - SLOTS_LO) * HALF;
+}
+}  // namespace g12m
+
+// (hi, lo) fp16 pair of an fp32 value: hi in the low half (k-pair element 2c), lo in the high half
+__device__ __forceinline__ uint32_t h2_split(float v) {
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(v - __half2float(hi));
+    return (uint32_t)__half_as_ushort(hi) | ((uint32_t)__half_as_ushort(lo) << 16);
+}
+
+// the hi (or lo) fp16 part of v, in both halves
+__device__ __forceinline__ uint32_t h2_dup_part(float v, bool lo) {
+    const __half hi = __float2half_rn(v);
+    const __half pt = lo ? __float2half_rn(v - __half2float(hi)) : hi;
+    const uint32_t u = __half_as_ushort(pt);
+    return u | (u << 16);
+}
+
+// the hi (or lo) parts of a and b as one pair (a low, b high)
+__device__ __forceinline__ uint32_t h2_pair_part(float a, float b, bool lo) {
+    const __half ah = __float2half_rn(a), bh = __float2half_rn(b);
+    const __half ap = lo ? __float2half_rn(a - __half2float(ah)) : ah;
+    const __half bp = lo ? __float2half_rn(b - __half2float(bh)) : bh;
+    return (uint32_t)__half_as_ushort(ap) | ((uint32_t)__half_as_ushort(bp) << 16);
+}
+
+// d += a . b on one m16n8k16 tile, fp16 operands, fp32 accumulators
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint4 lds_u32x4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds_u32x2m(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+// byte permute with the PTX selector semantics (a selector nibble with bit 3 set replicates the
+// sign bit of the selected byte)
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// (i_a - 8, i_b - 8) as fp16 from the low nibbles of bytes 0 and 2 (the i_z of two codes)
+__device__ __forceinline__ uint32_t zc8(uint32_t t) {
+    const uint32_t h = (t & 0x000F000Fu) | 0x64006400u;      // 1024 + i, exact
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x6408u),
+                                                                                  __ushort_as_half(0x6408u)));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+__device__ __forceinline__ uint32_t f2h2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Producer: half tiles in consumption order (K of tile t, then V of tile t) into the ring.
+__device__ void produce_g12m(const AttnParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty) {
+    using namespace g12m;
+    int seq = 0, s = 0;
+    uint32_t phase = 0;                                   // phase of slot s's next fill
+    bool ok = true;
+    WorkCursor wc = work_begin(p);
+    ItemRange r;
+    while (ok && work_next<true>(p, wc, r)) {
+        const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.kvh * p.kv_hs) * 2;
+        for (int t0 = r.tok0; t0 < r.tok1 && ok; t0 += TT) {
+            const uint32_t bytes = (uint32_t)min(TT, r.tok1 - t0) * 64u;
+            const int64_t off = base + (int64_t)t0 * 64;
+            #pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+                if (seq >= SLOTS && !mbar_wait(&empty[s], phase ^ 1u, kErrWaitEmpty)) { ok = false; break; }
+                mbar_arrive_expect_tx(&full[s], bytes);
+                bulk_g2s(smem + ring_off(s), (h ? p.vc : p.kc) + off, bytes, &full[s]);
+                ++seq;
+                if (++s == SLOTS) { s = 0; phase ^= 1u; }
+            }
+        }
+    }
+    const int issued = seq;                               // drain before the CTA may exit
+    for (int q = max(0, issued - SLOTS); q < issued; ++q)
+        mbar_wait(&full[q % SLOTS], (q / SLOTS) & 1, kErrWaitDrain);
+}
+
+__global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(AttnParams p) {
+    using namespace g12m;
+    extern __shared__ __align__(128) uint8_t g12m_smem[];
+    uint8_t* smem = g12m_smem;
+    float* sQ = reinterpret_cast<float*>(smem + OFF_Q);
+    float* sQraw = reinterpret_cast<float*>(smem + OFF_QRAW);
+    float* sWm = reinterpret_cast<float*>(smem + OFF_WML);
+    float* sWl = sWm + W * HQ;
+    float* sFin = reinterpret_cast<float*>(smem + OFF_FIN);
+    float* sAcc = reinterpret_cast<float*>(smem + OFF_ACC);
+    float* sM = reinterpret_cast<float*>(smem + OFF_MISC);
+    float* sL = sM + 4;
+    float* sC = sM + 8;
+    int* sflag = reinterpret_cast<int*>(sM + 12);
+    float* sAmax = sM + 16;                               // [W]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* empty = full + SLOTS;
+    uint64_t* rbar = empty + SLOTS;
+    const float* sR = reinterpret_cast<const float*>(smem + OFF_R);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t smem_base = (uint32_t)__cvta_generic_to_shared(smem);
+    const uint32_t tab_addr = smem_base + OFF_TAB;
+    if ((tab_addr & 0xFFFFu) != 0u) {                     // the window moved: refuse, loudly
+        if (tid == 0) flag_error(kErrSmemLayout);
+        return;
+    }
+    const float dr = p.r_max / 15.f;
+    const float z0 = __ldg(p.dec_z), dz = __ldg(p.dec_z + 1) - z0;      // uniform z bins: z = z0 + i dz
+
+    if (tid == 0) {
+        for (int s = 0; s < SLOTS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], W);
+        }
+        mbar_init(rbar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(rbar, RBYTES);              // R stays resident for every item
+        bulk_g2s(smem + OFF_R, p.R, RBYTES, rbar);
+    }
+    // the ring starts zeroed, so a partial tile's tail never holds bytes that decode to NaN
+    for (int i = tid; i < SLOTS * HALF / 16; i += blockDim.x) {
+        const int sl = i / (HALF / 16), o = i % (HALF / 16);
+        reinterpret_cast<uint4*>(smem + ring_off(sl))[o] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();                             // before the bulk copies overwrite it
+    // (x, y) table: row e = (i_r << 4) | i_theta, 32 copies of ((x_hi, x_lo), (y_hi, y_lo)) with
+    // (x, y) = i_r dr (cos, sin)(theta_i), theta_i = i / 15 * 2 pi - pi (stacked_plane.py:307)
+    {
+        uint2* tab = reinterpret_cast<uint2*>(smem + OFF_TAB);
+        const float drs = dr * 0.0625f;
+        for (int i = tid; i < 256 * 32; i += blockDim.x) {
+            const int e = i >> 5;
+            const float th = (float)(e & 15) / 15.f * 6.283185307179586f - 3.141592653589793f;
+            const float rr = (float)(e & 0xF0);
+            tab[i] = make_uint2(h2_split(rr * (cosf(th) * drs)), h2_split(rr * (sinf(th) * drs)));
+        }
+    }
+    float qreg = 0.f;                                     // the first item's queries, ahead of the stream
+    {
+        WorkCursor pc = work_begin(p);
+        ItemRange r0;
+        if (tid < HQ * 96 && work_next<true>(p, pc, r0))
+            qreg = q_load(p.q, p.qdt, (int64_t)r0.b * p.q_bs + (int64_t)(r0.hk * HQ + tid / 96) * p.q_hs + tid % 96);
+    }
+    __syncthreads();
+    if (warp == W) {
+        if (lane == 0) produce_g12m(p, smem, full, empty);
+        return;
+    }
+
+    constexpr int nthr = W * 32;
+    const int g = lane >> 2, c = lane & 3, hp = c & 1;
+    const bool lo_col = g >= 4;                           // this lane's operand column is a lo part
+    const int qh = g & 3;                                 // ... of head qh
+    const int rho = (g >> 1) + 4 * (g & 1);               // score rows g, g + 8: tokens rho, rho + 8
+    const uint32_t lanereg = tab_addr | ((uint32_t)lane << 3);
+    const uint32_t k_lane = (uint32_t)(rho * 64 + c * 16);
+    const uint32_t v_lane = (uint32_t)(c * 64 + g * 8);
+    int slot = 0;                                         // ring slot of the next half tile, its fill phase
+    uint32_t phase = 0;
+    bool alive = true;
+    if (!mbar_wait(rbar, 0, kErrWaitFull)) alive = false;
+    WorkCursor wc = work_begin(p);
+    ItemRange r;
+    while (work_next<true>(p, wc, r)) {
+        const int ntok = r.tok1 - r.tok0;
+        const int ntiles = (ntok + TT - 1) / TT;
+        if (tid < HQ * 96) sQraw[tid] = qreg;
+        named_bar_sync(1, nthr);
+        // q'_h = scale log2(e) R q_h: one warp per row k, lanes over the input index; the four
+        // heads' sums finish in a transpose-reduce, then a butterfly over the low three lane bits
+        #pragma unroll 1
+        for (int k = warp; k < 96; k += W) {
+            const float* row = sR + k * 96;
+            const float r0 = row[lane], r1 = row[lane + 32], r2 = row[lane + 64];
+            float a[HQ];
+            #pragma unroll
+            for (int h = 0; h < HQ; ++h)
+                a[h] = fmaf(r0, sQraw[h * 96 + lane], fmaf(r1, sQraw[h * 96 + lane + 32], r2 * sQraw[h * 96 + lane + 64]));
+            const bool up16 = (lane & 16) != 0;
+            const float k0 = up16 ? a[2] : a[0], k1 = up16 ? a[3] : a[1];
+            const float s0 = up16 ? a[0] : a[2], s1 = up16 ? a[1] : a[3];
+            float b0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 16);
+            float b1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 16);
+            const bool up8 = (lane & 8) != 0;
+            float v = (up8 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, up8 ? b0 : b1, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            if ((lane & 7) == 0) sQ[((lane >> 3) & 3) * 96 + k] = v * p.scale_log2;
+        }
+        named_bar_sync(1, nthr);
+        // largest operand magnitude: |q'_x|, |q'_y| and |q'_z| dz
+        {
+            float a = 0.f;
+            if (tid < HQ * 96) a = fabsf(sQ[tid]) * ((tid % 3 == 0) ? fabsf(dz) : 1.f);
+            #pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
+            if (lane == 0) sAmax[warp] = a;
+        }
+        // C_h = z0 sum_j q'_h,z,j (true log2 units)
+        if (warp < HQ) {
+            float cz = sQ[warp * 96 + 3 * lane];
+            #pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) cz += __shfl_xor_sync(0xffffffffu, cz, off);
+            if (lane == 0) sC[warp] = cz * z0;
+        }
+        named_bar_sync(1, nthr);
+        // power-of-two operand scale su = 2^k putting the largest magnitude in [2^13, 2^14)
+        float su = 1.f, us = 1.f;
+        {
+            float amax = 0.f;
+            #pragma unroll
+            for (int w = 0; w < W; ++w) amax = fmaxf(amax, sAmax[w]);
+            if (amax > 0.f && amax <= 3.0e38f) {
+                const int e = (int)((__float_as_uint(amax) >> 23) & 0xFF) - 127;   // floor(log2 amax), normal amax
+                const int k = max(-120, min(120, 13 - max(e, -126)));
+                su = __uint_as_float((uint32_t)(127 + k) << 23);
+                us = __uint_as_float((uint32_t)(127 - k) << 23);
+            }
+        }
+        // score operand fragments of this lane: column g (head qh, part lo_col), k-pairs as above
+        uint32_t bq[8][2], bz[2][2];
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int t = 8 * c + j;
+            bq[j][0] = h2_dup_part(sQ[qh * 96 + 3 * t + 1] * su, lo_col);
+            bq[j][1] = h2_dup_part(sQ[qh * 96 + 3 * t + 2] * su, lo_col);
+        }
+        #pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int t = 8 * c + 4 * j;
+            const float sz = su * dz;
+            bz[j][0] = h2_pair_part(sQ[qh * 96 + 3 * t] * sz, sQ[qh * 96 + 3 * (t + 1)] * sz, lo_col);
+            bz[j][1] = h2_pair_part(sQ[qh * 96 + 3 * (t + 2)] * sz, sQ[qh * 96 + 3 * (t + 3)] * sz, lo_col);
+        }
+        // softmax state of this lane's heads 2 hp, 2 hp + 1 (true log2 units)
+        const float cz0 = sC[2 * hp], cz1 = sC[2 * hp + 1];
+        float M0 = -INFINITY, M1 = -INFINITY;
+        float thr0 = -INFINITY, thr1 = -INFINITY;         // score-tile value above which M grows
+        f32x2 negoff = f2_pack(-INFINITY, -INFINITY);     // cz + 12 - M, or -inf while M is
+        const f32x2 uu = f2_pack(us, us);
+        f32x2 lsum = f2_pack(0.f, 0.f);
+        float acc[6][4];
+        #pragma unroll
+        for (int m = 0; m < 6; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
+
+        for (int tile = 0; tile < ntiles; ++tile) {
+            const int nt = min(TT, ntok - tile * TT);
+            const int wt0 = warp * TW;                      // this warp's first token of the tile
+            // ---- scores of 16 tokens x 8 columns ----------------------------------------
+            int s = slot;
+            if (alive && !mbar_wait(&full[s], phase, kErrWaitFull)) alive = false;
+            alive = __all_sync(0xffffffffu, alive);       // the tiles below are warp-collective
+            const bool act = alive && wt0 < nt;
+            float T[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            if (act) {
+                const uint32_t kb = smem_base + ring_off(s) + wt0 * 64 + k_lane;
+                const uint4 w0 = lds_u32x4(kb), w1 = lds_u32x4(kb + 512);
+                const uint32_t kw0[4] = {w0.x, w0.y, w0.z, w0.w}, kw1[4] = {w1.x, w1.y, w1.z, w1.w};
+                float sxy[4] = {0.f, 0.f, 0.f, 0.f}, sz[4] = {0.f, 0.f, 0.f, 0.f};
+                #pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t sel = (j & 1) ? 0x7624u : 0x7604u;
+                    const uint2 e0 = lds_u32x2m(__byte_perm(kw0[j >> 1], lanereg, sel));
+                    const uint2 e1 = lds_u32x2m(__byte_perm(kw1[j >> 1], lanereg, sel));
+                    mma16816(sxy, e0.x, e1.x, e0.y, e1.y, bq[j][0], bq[j][1]);
+                }
+                #pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    // (i_z of the low code, i_z of the high code) as fp16 subnormals i_z 2^-24
+                    // (bytes 1 and 3 of the word, zero bytes from the second operand)
+                    const uint32_t a0 = prmt(kw0[2 * j], 0u, 0x4341u), a1 = prmt(kw1[2 * j], 0u, 0x4341u);
+                    const uint32_t a2 = prmt(kw0[2 * j + 1], 0u, 0x4341u), a3 = prmt(kw1[2 * j + 1], 0u, 0x4341u);
+                    mma16816(sz, a0, a1, a2, a3, bz[j][0], bz[j][1]);
+                }
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) T[i] = fmaf(sz[i], 16777216.f, sxy[i]);
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) T[i] += __shfl_xor_sync(0xffffffffu, T[i], 2);   // hi + lo columns
+                if (wt0 + rho >= nt) T[0] = T[1] = -INFINITY;
+                if (wt0 + rho + 8 >= nt) T[2] = T[3] = -INFINITY;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++slot == SLOTS) { slot = 0; phase ^= 1u; }
+            // ---- online softmax per head ------------------------------------------------
+            uint32_t pA = 0u, pB = 0u;                       // weight fragments after the transposes
+            if (act) {
+                if (__any_sync(0xffffffffu, T[0] > thr0 || T[2] > thr0 || T[1] > thr1 || T[3] > thr1)) {
+                    float mx0 = fmaxf(T[0], T[2]), mx1 = fmaxf(T[1], T[3]);
+                    #pragma unroll
+                    for (int off = 4; off <= 16; off <<= 1) {
+                        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                    }
+                    const float n0 = fmaxf(M0, fmaf(mx0, us, cz0)), n1 = fmaxf(M1, fmaf(mx1, us, cz1));
+                    const float f0 = (M0 == -INFINITY) ? 0.f : fast_exp2(M0 - n0);
+                    const float f1 = (M1 == -INFINITY) ? 0.f : fast_exp2(M1 - n1);
+                    const f32x2 ff = f2_pack(f0, f1);
+                    lsum = f2_mul(lsum, ff);
+                    #pragma unroll
+                    for (int m = 0; m < 6; ++m) {
+                        acc[m][0] *= f0; acc[m][1] *= f1; acc[m][2] *= f0; acc[m][3] *= f1;
+                    }
+                    M0 = n0; M1 = n1;
+                    thr0 = (M0 - cz0) * su; thr1 = (M1 - cz1) * su;
+                    negoff = f2_pack(M0 == -INFINITY ? -INFINITY : cz0 + 12.f - M0,
+                                     M1 == -INFINITY ? -INFINITY : cz1 + 12.f - M1);
+                }
+                const float2 e01 = f2_unpack(f2_fma(f2_pack(T[0], T[1]), uu, negoff));
+                const float2 e23 = f2_unpack(f2_fma(f2_pack(T[2], T[3]), uu, negoff));
+                const float p0 = fast_exp2(e01.x), p1 = fast_exp2(e01.y), p2 = fast_exp2(e23.x), p3 = fast_exp2(e23.y);
+                lsum = f2_add(lsum, f2_add(f2_pack(p0, p1), f2_pack(p2, p3)));
+                // hi parts for the columns h < 4, lo parts for the columns h + 4 (no branch: the
+                // transposes below need the whole warp converged)
+                const uint32_t hA = f2h2(p0, p1), hB = f2h2(p2, p3);
+                const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&hA));
+                const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&hB));
+                const uint32_t lA = f2h2(p0 - fa.x, p1 - fa.y), lB = f2h2(p2 - fb.x, p3 - fb.y);
+                const uint32_t wA = (c >= 2) ? lA : hA, wB = (c >= 2) ? lB : hB;
+                pA = movmatrix_t(wA);                           // column g of tokens (c, c + 4)
+                pB = movmatrix_t(wB);                           // column g of tokens (c + 8, c + 12)
+            }
+            // ---- values: 6 m-tiles (x/y of triplets 4g + m; z of 4g .. 4g + 3) ---------------
+            s = slot;
+            if (alive && !mbar_wait(&full[s], phase, kErrWaitFull)) alive = false;
+            alive = __all_sync(0xffffffffu, alive);
+            if (act && alive) {
+                const uint32_t vb = smem_base + ring_off(s) + wt0 * 64 + v_lane;
+                uint2 vw[4];
+                #pragma unroll
+                for (int t = 0; t < 4; ++t) vw[t] = lds_u32x2m(vb + t * 256);     // tokens c + 4 t
+                const uint32_t d0 = __byte_perm(pA, 0u, 0x1010u), d1 = __byte_perm(pA, 0u, 0x3232u);
+                const uint32_t d2 = __byte_perm(pB, 0u, 0x1010u), d3 = __byte_perm(pB, 0u, 0x3232u);
+                #pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    const uint32_t sel = (m & 1) ? 0x7624u : 0x7604u;
+                    const uint2 x0 = lds_u32x2m(__byte_perm((m >> 1) ? vw[0].y : vw[0].x, lanereg, sel));
+                    const uint2 x1 = lds_u32x2m(__byte_perm((m >> 1) ? vw[1].y : vw[1].x, lanereg, sel));
+                    const uint2 x2 = lds_u32x2m(__byte_perm((m >> 1) ? vw[2].y : vw[2].x, lanereg, sel));
+                    const uint2 x3 = lds_u32x2m(__byte_perm((m >> 1) ? vw[3].y : vw[3].x, lanereg, sel));
+                    mma16816(acc[m], x0.x, x0.y, x1.x, x1.y, d0, d1);
+                    mma16816(acc[m], x2.x, x2.y, x3.x, x3.y, d2, d3);
+                }
+                #pragma unroll
+                for (int m = 0; m < 2; ++m) {
+                    const uint32_t wa = m ? vw[0].y : vw[0].x, wb = m ? vw[1].y : vw[1].x;
+                    const uint32_t wc2 = m ? vw[2].y : vw[2].x, wd = m ? vw[3].y : vw[3].x;
+                    // i_z - 8 of two tokens' codes as exact fp16 (1024 + i_z, less 1032): centred, so
+                    // that sum p (i_z - 8) does not grow tile by tile -- o_z = (z0 + 8 dz) l + dz
+                    // sum p (i_z - 8) then has no cancellation for the truncating tensor-core sums
+                    // to expose.  The tile's sums start from zero and join the running sums by
+                    // fp32 adds.
+                    float zt[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(zt, zc8(prmt(wa, wb, 0x5511u)), zc8(prmt(wa, wb, 0x7733u)),
+                             zc8(prmt(wc2, wd, 0x5511u)), zc8(prmt(wc2, wd, 0x7733u)), pA, pB);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[4 + m][i] += zt[i];
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (++slot == SLOTS) { slot = 0; phase ^= 1u; }
+        }
+        {                                                  // prefetch the next item's queries
+            WorkCursor pc = wc;
+            ItemRange rn;
+            if (tid < HQ * 96 && work_next<true>(p, pc, rn))
+                qreg = q_load(p.q, p.qdt, (int64_t)rn.b * p.q_bs + (int64_t)(rn.hk * HQ + tid / 96) * p.q_hs +
+                              tid % 96);
+        }
+        // ---- merge: hi + lo columns, the lanes of a warp, then the warps ----------------------
+        float2 lsf = f2_unpack(lsum);
+        #pragma unroll
+        for (int off = 4; off <= 16; off <<= 1) {
+            lsf.x += __shfl_xor_sync(0xffffffffu, lsf.x, off);
+            lsf.y += __shfl_xor_sync(0xffffffffu, lsf.y, off);
+        }
+        #pragma unroll
+        for (int m = 0; m < 6; ++m)
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) acc[m][i] += __shfl_xor_sync(0xffffffffu, acc[m][i], 2);
+        named_bar_sync(1, nthr);                           // every warp is done with sQ / sAcc of the last item
+        if (c < 2) {
+            float* o0 = sAcc + (warp * HQ + 2 * c) * 96;   // head 2c; head 2c + 1 at + 96
+            #pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int t = 4 * g + m;
+                o0[3 * t + 1] = acc[m][0]; o0[96 + 3 * t + 1] = acc[m][1];
+                o0[3 * t + 2] = acc[m][2]; o0[96 + 3 * t + 2] = acc[m][3];
+            }
+            #pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const int t = 4 * g + 2 * m;
+                o0[3 * t] = acc[4 + m][0]; o0[96 + 3 * t] = acc[4 + m][1];
+                o0[3 * (t + 1)] = acc[4 + m][2]; o0[96 + 3 * (t + 1)] = acc[4 + m][3];
+            }
+            if (g == 0) {
+                sWm[warp * HQ + 2 * c] = M0;
+                sWm[warp * HQ + 2 * c + 1] = M1;
+                sWl[warp * HQ + 2 * c] = lsf.x;
+                sWl[warp * HQ + 2 * c + 1] = lsf.y;
+            }
+        }
+        named_bar_sync(1, nthr);
+        for (int t = tid; t < HQ * 96; t += nthr) {
+            const int h = t / 96, k = t % 96;
+            float M = -INFINITY;
+            #pragma unroll
+            for (int w = 0; w < W; ++w) M = fmaxf(M, sWm[w * HQ + h]);
+            float v = 0.f, L = 0.f;
+            #pragma unroll
+            for (int w = 0; w < W; ++w) {
+                const float mw = sWm[w * HQ + h];
+                const float f = (mw == -INFINITY) ? 0.f : fast_exp2(mw - M);
+                v = fmaf(f, sAcc[w * HQ * 96 + h * 96 + k], v);
+                L = fmaf(f, sWl[w * HQ + h], L);
+            }
+            // z: sum p (z0 + dz i_z) = (z0 + 8 dz) l + dz sum p (i_z - 8)
+            if (k % 3 == 0) v = fmaf(dz, v, fmaf(8.f, dz, z0) * L);
+            // the weights carry 2^12 (2^12 exp2(s - M)): drop it, so that m is the running max
+            sAcc[h * 96 + k] = v * 0x1p-12f;               // warp 0's block: only this thread reads it
+            if (k == 0) {
+                sM[h] = M;
+                sL[h] = L * 0x1p-12f;
+            }
+        }
+        named_bar_sync(1, nthr);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 1);
+    }
+    xr_kernel_tail(p, tid, nthr);
+}
+
+}  // namespace pkv

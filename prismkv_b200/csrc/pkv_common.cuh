@@ -18,7 +18,8 @@ namespace pkv {
 __device__ int32_t g_device_error = 0;   // single definition: the library is one translation unit
 
 // 4: a split-sequence exchange waited past its bound for the other ranks' outputs
-enum : int32_t { kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3, kErrPeerWait = 4 };
+// 5: a kernel found its dynamic shared window at another address than its layout assumes
+enum : int32_t { kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3, kErrPeerWait = 4, kErrSmemLayout = 5 };
 
 __device__ __forceinline__ void flag_error(int32_t code) { atomicCAS(&g_device_error, 0, code); }
 

@@ -105,6 +105,7 @@ class SequenceExchange:
             q = q[:, :, 0, :]
         self.shape = tuple(q.shape)
         self.layout = self._layout(q, k_codes)
+        self._checked = set()
         self.owned, self.opened = [], []
         with torch.cuda.device(self.device):
             n_own = 1 if _single_world is None else self.world
@@ -159,9 +160,12 @@ class SequenceExchange:
             q = q[:, :, 0, :]
         if tuple(q.shape) != self.shape:
             raise ValueError(f"exchange built for queries {self.shape}, got {tuple(q.shape)}")
-        lay = self._layout(q, k_codes)
-        if (lay.bytes, lay.units) != (self.layout.bytes, self.layout.units):
-            raise ValueError("this call's kernel plan splits the heads into other units than the exchange's")
+        key = (q.dtype, k_codes.dtype, tuple(k_codes.shape), num_splits)
+        if key not in self._checked:                      # plan each call shape once
+            lay = self._layout(q, k_codes)
+            if (lay.bytes, lay.units) != (self.layout.bytes, self.layout.units):
+                raise ValueError("this call's kernel plan splits the heads into other units than the exchange's")
+            self._checked.add(key)
         self.codec.attention(q, k_codes, v_codes, scale=scale, num_splits=num_splits, exchange=self)
         return self.out
 

@@ -120,9 +120,18 @@ def test_attention_matches_oracle(cuda_ready, B, Hq, Hkv, S, variant, bits, qdt,
     out = decode_attention(q, qv, kc, vc, num_splits=splits)
     ref = oracle.attention(qv.float().cpu().numpy(), kc.cpu().numpy().astype(np.int64),
                            vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
-    plan = q.codec(torch.device(DEV)).describe(qv, kc, vc)
+    codec = q.codec(torch.device(DEV))
+    plan = codec.describe(qv, kc, vc)
     tol = TOL_TC if plan["kernel"] == "attn_tc_kernel" else TOL
     np.testing.assert_allclose(out.cpu().numpy(), ref, atol=tol, rtol=0)
+    if plan["kernel"] == "attn_gqa12_mma_kernel":          # and the same groups on the fp32 kernel
+        codec.fp32_attention = True
+        try:
+            assert codec.describe(qv, kc, vc)["kernel"] == "attn_gqa12_kernel"
+            out32 = decode_attention(q, qv, kc, vc, num_splits=splits)
+        finally:
+            codec.fp32_attention = False
+        np.testing.assert_allclose(out32.cpu().numpy(), ref, atol=TOL, rtol=0)
 
 
 @pytest.mark.parametrize("dim", [66, 192, 129])
@@ -231,10 +240,10 @@ def test_attention_shapes_in_turn_share_workspace(cuda_ready):
 
 @pytest.mark.parametrize("B,Hq,Hkv,S,variant,bits,kernel", [
     (8, 32, 32, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),
-    (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_gqa12_kernel"),        # grouped heads: four per unit
+    (4, 32, 8, 4096, "v1", (4, 4, 4), "attn_gqa12_mma_kernel"),    # grouped heads: four per unit
     (4, 16, 8, 4096, "v1", (4, 4, 4), "attn_mha12_kernel"),        # group 2: one query head per unit
     (1, 8, 8, 4097, "v1", (4, 4, 4), "attn_mha12_stream_kernel"),
-    (4, 32, 8, 131072, "v1", (4, 4, 4), "attn_gqa12_kernel"),
+    (4, 32, 8, 131072, "v1", (4, 4, 4), "attn_gqa12_mma_kernel"),
     (2, 8, 8, 4096, "v1", (3, 3, 2), "attn_mha8_kernel"),
     (2, 32, 8, 4096, "v1", (3, 3, 2), "attn_mha8_kernel"),        # fp32 queries of a group
     (2, 8, 8, 4096, "v1", (2, 3, 3), "attn_polar_kernel"),
@@ -248,6 +257,59 @@ def test_attention_plan_picks_kernel(cuda_ready, B, Hq, Hkv, S, variant, bits, k
     plan = q.codec(torch.device(DEV)).describe(torch.zeros(B, Hq, 96, device=DEV), kc, kc)
     assert plan["kernel"] == kernel
     assert plan["num_splits"] >= 1 and plan["smem_bytes"] <= 227 * 1024
+
+
+def test_fp32_flag_plans_the_fp32_grouped_kernel(cuda_ready):
+    q, _ = _setup("v1", (4, 4, 4))
+    kc = torch.zeros(4, 8, 4096, q.m, dtype=q.code_dtype, device=DEV)
+    codec = q.codec(torch.device(DEV))
+    qv = torch.zeros(4, 32, 96, device=DEV)
+    codec.fp32_attention = True
+    try:
+        assert codec.describe(qv, kc, kc)["kernel"] == "attn_gqa12_kernel"
+    finally:
+        codec.fp32_attention = False
+    assert codec.describe(qv, kc, kc)["kernel"] == "attn_gqa12_mma_kernel"
+
+
+def _ref_attention(q, p, qv, kc, vc):
+    return oracle.attention(qv.float().cpu().numpy(), kc.cpu().numpy().astype(np.int64),
+                            vc.cpu().numpy().astype(np.int64), q.R.numpy(), p)
+
+
+@pytest.mark.parametrize("case", ["huge_q", "tiny_q", "zero_q", "peaked", "one_token", "two_tokens", "mixed_rows"])
+def test_grouped_tensor_core_numerics(cuda_ready, case):
+    """The fp16-pair tensor-core kernel at the edges of its operand scaling: queries of 1e4 and of
+    1e-7 (the per-item power-of-two scale), all-zero queries (uniform weights), one key far above
+    the rest (weights down to exp2(-30) of the largest), one and two tokens (no averaging of
+    rounding), and rows of very different scales in one call.  Max error 1e-3 against the oracle."""
+    q, p = _setup("v1", (4, 4, 4))
+    S = {"one_token": 1, "two_tokens": 2}.get(case, 700)
+    B, Hq, Hkv = 2, 8, 2
+    kc, vc = _codes(q, B, Hkv, S, seed=91)
+    g = torch.Generator(device=DEV).manual_seed(92)
+    qv = torch.randn(B, Hq, 96, generator=g, device=DEV)
+    if case == "huge_q":
+        qv *= 1e4
+    elif case == "tiny_q":
+        qv *= 1e-7
+    elif case == "zero_q":
+        qv.zero_()
+    elif case == "peaked":
+        # the query of every head points along key token 5 of its KV head (decoded), scaled so
+        # that token's score leads the others by about 30 (log2 units)
+        kd = q.decode(kc[:, :, 5].reshape(-1, q.m)).view(B, Hkv, 96)
+        qv = kd.repeat_interleave(Hq // Hkv, dim=1) * 3.0
+    elif case == "mixed_rows":
+        qv[0] *= 1e3
+        qv[1] *= 1e-3
+    codec = q.codec(torch.device(DEV))
+    assert codec.describe(qv, kc, vc)["kernel"] == "attn_gqa12_mma_kernel"
+    out = decode_attention(q, qv, kc, vc)
+    ref = _ref_attention(q, p, qv, kc, vc)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, atol=TOL, rtol=0)
+    from prismkv_b200 import _lib
+    assert _lib.device_error() == 0
 
 
 def test_attention_balanced_schedule(cuda_ready):
@@ -303,21 +365,32 @@ def test_aggressive_decode_full_size(cuda_ready):
 
 def test_longctx_full_size_with_outliers(cuda_ready):
     """The split-sequence workload at full size on one GPU (B=4, 32 query / 8 KV heads, S=131072,
-    1 % of the channels x8 before the rotation) through the grouped 12-bit kernel; two (batch,
-    KV head) units -- eight query heads -- against the oracle at the fp32 bound."""
+    1 % of the channels x8 before the rotation) through the grouped 12-bit kernels (tensor-core
+    and fp32); two (batch, KV head) units -- eight query heads -- against the oracle at the fp32
+    bound, and all units of the two kernels against each other."""
     from prismkv_b200.synthetic import WORKLOADS, make_kv_codes, make_query, make_quantizer
     w = WORKLOADS["longctx-splitseq"]
     q = make_quantizer(w)
     kc, vc = make_kv_codes(w, q, DEV)
     qv = make_query(w, DEV)
-    assert q.codec(torch.device(DEV)).describe(qv, kc, vc)["kernel"] == "attn_gqa12_kernel"
+    codec = q.codec(torch.device(DEV))
+    assert codec.describe(qv, kc, vc)["kernel"] == "attn_gqa12_mma_kernel"
     out = decode_attention(q, qv, kc, vc)
+    codec.fp32_attention = True
+    try:
+        assert codec.describe(qv, kc, vc)["kernel"] == "attn_gqa12_kernel"
+        out32 = decode_attention(q, qv, kc, vc)
+    finally:
+        codec.fp32_attention = False
     p = oracle.QuantParams.default(96)
     for b, hk in ((0, 0), (3, 7)):
         ref = oracle.attention(qv[b:b + 1, 4 * hk:4 * hk + 4].float().cpu().numpy(),
                                kc[b:b + 1, hk:hk + 1].cpu().numpy().astype(np.int64),
                                vc[b:b + 1, hk:hk + 1].cpu().numpy().astype(np.int64), q.R.numpy(), p)
-        np.testing.assert_allclose(out[b:b + 1, 4 * hk:4 * hk + 4].cpu().numpy(), ref, atol=TOL, rtol=0)
+        for o in (out, out32):
+            np.testing.assert_allclose(o[b:b + 1, 4 * hk:4 * hk + 4].cpu().numpy(), ref, atol=TOL, rtol=0)
+    # every unit: the two kernels agree far inside the bound
+    np.testing.assert_allclose(out.cpu().numpy(), out32.cpu().numpy(), atol=1e-4, rtol=0)
     from prismkv_b200 import _lib
     assert _lib.device_error() == 0
 

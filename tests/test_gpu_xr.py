@@ -41,8 +41,9 @@ def _data(q, B, Hq, Hkv, S, qdt, seed):
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,S,bits,variant,qdt,kernel", [
-    (2, 16, 4, 3000, (4, 4, 4), "v1", torch.bfloat16, "attn_gqa12_kernel"),
-    (1, 32, 8, 20000, (4, 4, 4), "v1", torch.float32, "attn_gqa12_kernel"),       # balanced segments
+    (2, 16, 4, 3000, (4, 4, 4), "v1", torch.bfloat16, "attn_gqa12_mma_kernel"),
+    (1, 32, 8, 20000, (4, 4, 4), "v1", torch.float32, "attn_gqa12_mma_kernel"),   # balanced segments
+    (1, 32, 8, 20000, (4, 4, 4), "fp32", torch.float32, "attn_gqa12_kernel"),
     (2, 8, 8, 3000, (4, 4, 4), "v1", torch.float32, "attn_mha12_kernel"),
     (2, 8, 8, 6000, (4, 4, 4), "v1", torch.bfloat16, "attn_mha12_stream_kernel"),
     (2, 8, 8, 3000, (3, 3, 2), "v1", torch.float32, "attn_mha8_kernel"),
@@ -54,6 +55,7 @@ def test_one_rank_exchange_matches_unsplit(cuda_ready, B, Hq, Hkv, S, bits, vari
     q = _quantizer(bits, variant)
     qv, kc, vc = _data(q, B, Hq, Hkv, S, qdt, seed=S + Hq)
     codec = q.codec(torch.device(DEV))
+    codec.fp32_attention = variant == "fp32"                 # this test's own quantizer: no restore
     if kernel is not None:
         assert codec.describe(qv, kc, vc)["kernel"] == kernel
     ref = codec.attention(qv, kc, vc)

@@ -12,14 +12,16 @@ from prismkv_b200 import _lib
 ALIGNED = 1 << 12                # stand-in device addresses: planning never dereferences them
 
 
-def _codec(bits=(4, 4, 4), learned=False, bias=False, lloyd=False):
+def _codec(bits=(4, 4, 4), learned=False, bias=False, lloyd=False, fp32=False, r_max=9.8):
     c = _lib.PkvCodec()
     c.dim = 96
     c.bits_z, c.bits_r, c.bits_theta = bits
     c.xy_mode = 1 if learned else 0
     c.xy_per_z = 1 if (learned or bias) else 0
-    c.r_max = 9.8
+    c.r_max = r_max
     c.flags = 0 if (learned or bias or lloyd) else _lib.PKV_CODEC_Z_UNIFORM
+    if fp32:
+        c.flags |= _lib.PKV_CODEC_FP32_ATTN
     c.R = c.z_thr = c.r2_thr = c.th_thr = c.dec_z = c.dec_xy = ALIGNED
     c.codebook = ALIGNED if learned else None
     c.bias_xy = ALIGNED if bias else None
@@ -53,9 +55,13 @@ BF16 = _lib.PKV_BF16
     ("phi3-decode", {}, (8, 32, 32, 4096, (4, 4, 4), BF16), "attn_mha12_kernel"),
     ("aggressive-332", dict(bits=(3, 3, 2)), (32, 32, 32, 16384, (3, 3, 2), BF16), "attn_mha8_kernel"),
     ("learned-gqa", dict(learned=True, bias=True), (16, 32, 8, 32768, (4, 4, 4), BF16), "attn_tc_kernel"),
-    ("longctx-splitseq", {}, (4, 32, 8, 131072, (4, 4, 4), BF16), "attn_gqa12_kernel"),
-    ("longctx, one rank of eight", {}, (4, 32, 8, 16384, (4, 4, 4), BF16), "attn_gqa12_kernel"),
-    ("group 8, 12-bit, fp32", {}, (2, 16, 2, 3000, (4, 4, 4), _lib.PKV_F32), "attn_gqa12_kernel"),
+    ("longctx-splitseq", {}, (4, 32, 8, 131072, (4, 4, 4), BF16), "attn_gqa12_mma_kernel"),
+    ("longctx, one rank of eight", {}, (4, 32, 8, 16384, (4, 4, 4), BF16), "attn_gqa12_mma_kernel"),
+    ("group 8, 12-bit, fp32", {}, (2, 16, 2, 3000, (4, 4, 4), _lib.PKV_F32), "attn_gqa12_mma_kernel"),
+    ("longctx, fp32 arithmetic asked for", dict(fp32=True), (4, 32, 8, 131072, (4, 4, 4), BF16),
+     "attn_gqa12_kernel"),
+    ("longctx, radii past the fp16 pairs", dict(r_max=1e5), (4, 32, 8, 131072, (4, 4, 4), BF16),
+     "attn_gqa12_kernel"),
     ("group 2, 12-bit: one query head per unit", {}, (2, 8, 4, 3000, (4, 4, 4), BF16), "attn_mha12_kernel"),
     ("group 2, long: one query head per unit", {}, (2, 8, 4, 9000, (4, 4, 4), BF16), "attn_mha12_stream_kernel"),
     ("cpu-roundtrip", {}, (1, 8, 8, 1024, (4, 4, 4), _lib.PKV_F32), "attn_mha12_kernel"),
@@ -100,4 +106,6 @@ def test_one_head_kernels_fill_the_grid():
 def test_grouped_12bit_kernel_streams_balanced_ranges():
     """longctx (32 units of 131072 tokens on 148 SMs): every CTA streams an equal share of tiles."""
     p = _plan(_codec(), _args(4, 32, 8, 131072, (4, 4, 4), BF16))
+    assert p.balanced == 1 and p.smem_bytes <= 227 * 1024 and p.threads == 16 * 32
+    p = _plan(_codec(fp32=True), _args(4, 32, 8, 131072, (4, 4, 4), BF16))
     assert p.balanced == 1 and p.smem_bytes <= 227 * 1024 and p.threads == 20 * 32
