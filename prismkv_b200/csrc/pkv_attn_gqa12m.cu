@@ -47,40 +47,42 @@
 //
 // Work, ring and exchange as in attn_gqa12_kernel: one CTA per SM (15 consumer warps, one TMA
 // producer warp: four warps per SM sub-partition leave 128 registers a thread), persistent over
-// balanced tile ranges, half tiles (K or V codes of 240 tokens, 15 KB) through a ring of six
-// slots (four below the table, two above), bounded mbarrier waits, splits merged by the last CTA
-// (finish_item).
+// balanced tile ranges.  A warp owns two 16-token groups of every tile, interleaved, so that
+// each group's tiles hide the other's latencies and the ring bookkeeping is paid per 32 tokens.
+// Half tiles (K or V codes of 480 tokens, 30 KB) flow through a ring of four slots (two below the
+// table, two above), bounded mbarrier waits; splits merge in the last CTA (finish_item).  R is
+// read through L2 (the query rotation and the final o @ R), which leaves the room to the ring.
 
 namespace pkv {
 namespace g12m {
 constexpr int W = 15;                                   // consumer warps (16 warps: 128 registers)
 constexpr int HQ = 4;                                   // query heads per unit
-constexpr int TW = 16;                                  // tokens per warp per tile
+constexpr int NG = 2;                                   // 16-token groups per warp per tile
+constexpr int TW = 16 * NG;                             // tokens per warp per tile
 constexpr int TT = W * TW;                              // tokens per tile
 constexpr int HALF = TT * 64;                           // K (or V) codes of a tile: 32 x uint16 / token
-constexpr int SLOTS = 6;                                // ring of half tiles
+constexpr int SLOTS = 4;                                // ring of half tiles
+constexpr int PF = 2;                                   // tiles asked into L2 ahead of the ring
 constexpr int TAB_BYTES = 256 * 32 * 8;                 // [256 flat][32 copies] (x hi|lo, y hi|lo)
 // The dynamic shared window of a kernel without static shared memory starts at shared address
 // 0x400 on sm_100 (the first KB is reserved; checked at run time).  The table must start at a
-// 64 KB-aligned shared address, so it sits at window offset 0x10000 - 0x400; the four ring slots
-// and the queries fill the window below it, the rest (two more slots among it) lies above.
+// 64 KB-aligned shared address, so it sits at window offset 0x10000 - 0x400; two ring slots and
+// the queries fill the window below it, the rest (two more slots among it) lies above.
 constexpr uint32_t SMEM_BASE = 0x400;
 constexpr int OFF_TAB = (int)((0x10000u - (SMEM_BASE & 0xFFFFu)) & 0xFFFFu);
-constexpr int SLOTS_LO = 4;                             // ring slots below the table
+constexpr int SLOTS_LO = 2;                             // ring slots below the table
 constexpr int OFF_RING_LO = 0;
 constexpr int OFF_Q = OFF_RING_LO + SLOTS_LO * HALF;    // [4][96] rotated, scaled queries
 constexpr int OFF_QRAW = OFF_Q + HQ * 96 * 4;           // [4][96] raw queries
-constexpr int OFF_R = OFF_TAB + TAB_BYTES;              // R, fp32, row pitch 96 (resident)
-constexpr int RBYTES = 96 * 96 * 4;
-constexpr int OFF_ACC = OFF_R + RBYTES;                 // item merge [W][4][96]
+constexpr int OFF_ACC = OFF_TAB + TAB_BYTES;            // item merge [W][4][96]
 constexpr int OFF_WML = OFF_ACC + W * HQ * 96 * 4;      // [W][4] max, [W][4] sum
 constexpr int OFF_FIN = OFF_WML + 2 * W * HQ * 4;       // [4][96]
 constexpr int OFF_MISC = OFF_FIN + HQ * 96 * 4;         // sM[4], sL[4], sC[4], flag, amax[W]
-constexpr int OFF_BAR = OFF_MISC + 128;                 // full[SLOTS], empty[SLOTS], rbar
-constexpr int OFF_RING_HI = (OFF_BAR + (2 * SLOTS + 1) * 8 + 127) / 128 * 128;
+constexpr int OFF_BAR = OFF_MISC + 128;                 // full[SLOTS], empty[SLOTS]
+constexpr int OFF_RING_HI = (OFF_BAR + 2 * SLOTS * 8 + 127) / 128 * 128;
 constexpr int TOTAL = OFF_RING_HI + (SLOTS - SLOTS_LO) * HALF;
 static_assert(OFF_QRAW + HQ * 96 * 4 <= OFF_TAB, "slots and queries below the table");
-static_assert(OFF_R % 128 == 0 && OFF_ACC % 16 == 0 && OFF_BAR % 8 == 0 && HALF % 128 == 0, "alignment");
+static_assert(OFF_ACC % 16 == 0 && OFF_BAR % 8 == 0 && HALF % 128 == 0, "alignment");
 static_assert(TOTAL <= 227 * 1024, "one CTA per SM");
 static_assert(W * 32 >= HQ * 96, "one consumer thread per query element (the query prefetch)");
 
@@ -162,7 +164,10 @@ __device__ __forceinline__ uint32_t f2h2(float lo, float hi) {
     return r;
 }
 
-// Producer: half tiles in consumption order (K of tile t, then V of tile t) into the ring.
+// Producer: half tiles in consumption order (K of tile t, then V of tile t) into the ring.  The
+// ring holds three tiles; the codes of the next PF tiles of the item are asked into L2 ahead
+// (bulk prefetches, no shared memory), so that the copies into the ring meet L2 latency and the
+// memory system sees the ring's bytes plus PF tiles in flight per SM.
 __device__ void produce_g12m(const AttnParams& p, uint8_t* smem, uint64_t* full, uint64_t* empty) {
     using namespace g12m;
     int seq = 0, s = 0;
@@ -172,9 +177,20 @@ __device__ void produce_g12m(const AttnParams& p, uint8_t* smem, uint64_t* full,
     ItemRange r;
     while (ok && work_next<true>(p, wc, r)) {
         const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.kvh * p.kv_hs) * 2;
+        {
+            const uint32_t bytes = (uint32_t)min(PF * TT, r.tok1 - r.tok0) * 64u;
+            bulk_prefetch_l2(p.kc + base + (int64_t)r.tok0 * 64, bytes);
+            bulk_prefetch_l2(p.vc + base + (int64_t)r.tok0 * 64, bytes);
+        }
         for (int t0 = r.tok0; t0 < r.tok1 && ok; t0 += TT) {
             const uint32_t bytes = (uint32_t)min(TT, r.tok1 - t0) * 64u;
             const int64_t off = base + (int64_t)t0 * 64;
+            if (t0 + PF * TT < r.tok1) {
+                const int tp = t0 + PF * TT;
+                const uint32_t pbytes = (uint32_t)min(TT, r.tok1 - tp) * 64u;
+                bulk_prefetch_l2(p.kc + base + (int64_t)tp * 64, pbytes);
+                bulk_prefetch_l2(p.vc + base + (int64_t)tp * 64, pbytes);
+            }
             #pragma unroll 1
             for (int h = 0; h < 2; ++h) {
                 if (seq >= SLOTS && !mbar_wait(&empty[s], phase ^ 1u, kErrWaitEmpty)) { ok = false; break; }
@@ -207,8 +223,6 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
     float* sAmax = sM + 16;                               // [W]
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + SLOTS;
-    uint64_t* rbar = empty + SLOTS;
-    const float* sR = reinterpret_cast<const float*>(smem + OFF_R);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t smem_base = (uint32_t)__cvta_generic_to_shared(smem);
@@ -217,7 +231,6 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
         if (tid == 0) flag_error(kErrSmemLayout);
         return;
     }
-    const float dr = p.r_max / 15.f;
     const float z0 = __ldg(p.dec_z), dz = __ldg(p.dec_z + 1) - z0;      // uniform z bins: z = z0 + i dz
 
     if (tid == 0) {
@@ -225,10 +238,7 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], W);
         }
-        mbar_init(rbar, 1);
         fence_mbar_init();
-        mbar_arrive_expect_tx(rbar, RBYTES);              // R stays resident for every item
-        bulk_g2s(smem + OFF_R, p.R, RBYTES, rbar);
     }
     // the ring starts zeroed, so a partial tile's tail never holds bytes that decode to NaN
     for (int i = tid; i < SLOTS * HALF / 16; i += blockDim.x) {
@@ -236,16 +246,13 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
         reinterpret_cast<uint4*>(smem + ring_off(sl))[o] = make_uint4(0u, 0u, 0u, 0u);
     }
     fence_proxy_async_smem();                             // before the bulk copies overwrite it
-    // (x, y) table: row e = (i_r << 4) | i_theta, 32 copies of ((x_hi, x_lo), (y_hi, y_lo)) with
-    // (x, y) = i_r dr (cos, sin)(theta_i), theta_i = i / 15 * 2 pi - pi (stacked_plane.py:307)
+    // (x, y) table: row e = (i_r << 4) | i_theta, 32 copies of ((x_hi, x_lo), (y_hi, y_lo)) of the
+    // codec's decoded (x, y) of the flat index (the uniform polar grid, stacked_plane.py:297-310)
     {
         uint2* tab = reinterpret_cast<uint2*>(smem + OFF_TAB);
-        const float drs = dr * 0.0625f;
         for (int i = tid; i < 256 * 32; i += blockDim.x) {
-            const int e = i >> 5;
-            const float th = (float)(e & 15) / 15.f * 6.283185307179586f - 3.141592653589793f;
-            const float rr = (float)(e & 0xF0);
-            tab[i] = make_uint2(h2_split(rr * (cosf(th) * drs)), h2_split(rr * (sinf(th) * drs)));
+            const float2 xy = __ldg(reinterpret_cast<const float2*>(p.dec_xy) + (i >> 5));
+            tab[i] = make_uint2(h2_split(xy.x), h2_split(xy.y));
         }
     }
     float qreg = 0.f;                                     // the first item's queries, ahead of the stream
@@ -272,7 +279,6 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
     int slot = 0;                                         // ring slot of the next half tile, its fill phase
     uint32_t phase = 0;
     bool alive = true;
-    if (!mbar_wait(rbar, 0, kErrWaitFull)) alive = false;
     WorkCursor wc = work_begin(p);
     ItemRange r;
     while (work_next<true>(p, wc, r)) {
@@ -280,12 +286,13 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
         const int ntiles = (ntok + TT - 1) / TT;
         if (tid < HQ * 96) sQraw[tid] = qreg;
         named_bar_sync(1, nthr);
-        // q'_h = scale log2(e) R q_h: one warp per row k, lanes over the input index; the four
-        // heads' sums finish in a transpose-reduce, then a butterfly over the low three lane bits
+        // q'_h = scale log2(e) R q_h: one warp per row k of R (read through L2), lanes over the
+        // input index; the four heads' sums finish in a transpose-reduce, then a butterfly over
+        // the low three lane bits
         #pragma unroll 1
         for (int k = warp; k < 96; k += W) {
-            const float* row = sR + k * 96;
-            const float r0 = row[lane], r1 = row[lane + 32], r2 = row[lane + 64];
+            const float* row = p.R + k * 96;
+            const float r0 = __ldg(row + lane), r1 = __ldg(row + lane + 32), r2 = __ldg(row + lane + 64);
             float a[HQ];
             #pragma unroll
             for (int h = 0; h < HQ; ++h)
@@ -361,47 +368,79 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
         for (int tile = 0; tile < ntiles; ++tile) {
             const int nt = min(TT, ntok - tile * TT);
             const int wt0 = warp * TW;                      // this warp's first token of the tile
-            // ---- scores of 16 tokens x 8 columns ----------------------------------------
+            // ---- scores of 2 x 16 tokens x 8 columns ----------------------------------------
             int s = slot;
             if (alive && !mbar_wait(&full[s], phase, kErrWaitFull)) alive = false;
             alive = __all_sync(0xffffffffu, alive);       // the tiles below are warp-collective
             const bool act = alive && wt0 < nt;
-            float T[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+            float T[NG][4];
+            #pragma unroll
+            for (int gi = 0; gi < NG; ++gi) T[gi][0] = T[gi][1] = T[gi][2] = T[gi][3] = -INFINITY;
             if (act) {
                 const uint32_t kb = smem_base + ring_off(s) + wt0 * 64 + k_lane;
-                const uint4 w0 = lds_u32x4(kb), w1 = lds_u32x4(kb + 512);
-                const uint32_t kw0[4] = {w0.x, w0.y, w0.z, w0.w}, kw1[4] = {w1.x, w1.y, w1.z, w1.w};
-                float sxy[4] = {0.f, 0.f, 0.f, 0.f}, sz[4] = {0.f, 0.f, 0.f, 0.f};
+                uint32_t kw[NG][2][4];                      // [group][token rho / rho + 8][word]
+                #pragma unroll
+                for (int gi = 0; gi < NG; ++gi) {
+                    const uint4 w0 = lds_u32x4(kb + gi * 1024), w1 = lds_u32x4(kb + gi * 1024 + 512);
+                    kw[gi][0][0] = w0.x; kw[gi][0][1] = w0.y; kw[gi][0][2] = w0.z; kw[gi][0][3] = w0.w;
+                    kw[gi][1][0] = w1.x; kw[gi][1][1] = w1.y; kw[gi][1][2] = w1.z; kw[gi][1][3] = w1.w;
+                }
+                // per group two independent chains over the (x, y) steps (even / odd triplets), one for z
+                float sxa[NG][4], sxb[NG][4], sz[NG][4];
+                #pragma unroll
+                for (int gi = 0; gi < NG; ++gi)
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) sxa[gi][i] = sxb[gi][i] = sz[gi][i] = 0.f;
                 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const uint32_t sel = (j & 1) ? 0x7624u : 0x7604u;
-                    const uint2 e0 = lds_u32x2m(__byte_perm(kw0[j >> 1], lanereg, sel));
-                    const uint2 e1 = lds_u32x2m(__byte_perm(kw1[j >> 1], lanereg, sel));
-                    mma16816(sxy, e0.x, e1.x, e0.y, e1.y, bq[j][0], bq[j][1]);
+                    #pragma unroll
+                    for (int gi = 0; gi < NG; ++gi) {
+                        const uint2 e0 = lds_u32x2m(__byte_perm(kw[gi][0][j >> 1], lanereg, sel));
+                        const uint2 e1 = lds_u32x2m(__byte_perm(kw[gi][1][j >> 1], lanereg, sel));
+                        mma16816((j & 1) ? sxb[gi] : sxa[gi], e0.x, e1.x, e0.y, e1.y, bq[j][0], bq[j][1]);
+                    }
                 }
                 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    // (i_z of the low code, i_z of the high code) as fp16 subnormals i_z 2^-24
-                    // (bytes 1 and 3 of the word, zero bytes from the second operand)
-                    const uint32_t a0 = prmt(kw0[2 * j], 0u, 0x4341u), a1 = prmt(kw1[2 * j], 0u, 0x4341u);
-                    const uint32_t a2 = prmt(kw0[2 * j + 1], 0u, 0x4341u), a3 = prmt(kw1[2 * j + 1], 0u, 0x4341u);
-                    mma16816(sz, a0, a1, a2, a3, bz[j][0], bz[j][1]);
+                for (int j = 0; j < 2; ++j)
+                    #pragma unroll
+                    for (int gi = 0; gi < NG; ++gi) {
+                        // (i_z of the low code, i_z of the high code) as fp16 subnormals i_z 2^-24
+                        // (bytes 1 and 3 of the word, zero bytes from the second operand)
+                        mma16816(sz[gi], prmt(kw[gi][0][2 * j], 0u, 0x4341u), prmt(kw[gi][1][2 * j], 0u, 0x4341u),
+                                 prmt(kw[gi][0][2 * j + 1], 0u, 0x4341u), prmt(kw[gi][1][2 * j + 1], 0u, 0x4341u),
+                                 bz[j][0], bz[j][1]);
+                    }
+                #pragma unroll
+                for (int gi = 0; gi < NG; ++gi) {
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) T[gi][i] = fmaf(sz[gi][i], 16777216.f, sxa[gi][i] + sxb[gi][i]);
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) T[gi][i] += __shfl_xor_sync(0xffffffffu, T[gi][i], 2);   // hi + lo
+                    const int t0 = wt0 + 16 * gi + rho;
+                    if (t0 >= nt) T[gi][0] = T[gi][1] = -INFINITY;
+                    if (t0 + 8 >= nt) T[gi][2] = T[gi][3] = -INFINITY;
                 }
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) T[i] = fmaf(sz[i], 16777216.f, sxy[i]);
-                #pragma unroll
-                for (int i = 0; i < 4; ++i) T[i] += __shfl_xor_sync(0xffffffffu, T[i], 2);   // hi + lo columns
-                if (wt0 + rho >= nt) T[0] = T[1] = -INFINITY;
-                if (wt0 + rho + 8 >= nt) T[2] = T[3] = -INFINITY;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             if (++slot == SLOTS) { slot = 0; phase ^= 1u; }
             // ---- online softmax per head ------------------------------------------------
-            uint32_t pA = 0u, pB = 0u;                       // weight fragments after the transposes
+            uint32_t pA[NG], pB[NG];                        // weight fragments after the transposes
+            #pragma unroll
+            for (int gi = 0; gi < NG; ++gi) pA[gi] = pB[gi] = 0u;
             if (act) {
-                if (__any_sync(0xffffffffu, T[0] > thr0 || T[2] > thr0 || T[1] > thr1 || T[3] > thr1)) {
-                    float mx0 = fmaxf(T[0], T[2]), mx1 = fmaxf(T[1], T[3]);
+                bool up = false;
+                #pragma unroll
+                for (int gi = 0; gi < NG; ++gi)
+                    up = up || T[gi][0] > thr0 || T[gi][2] > thr0 || T[gi][1] > thr1 || T[gi][3] > thr1;
+                if (__any_sync(0xffffffffu, up)) {
+                    float mx0 = fmaxf(T[0][0], T[0][2]), mx1 = fmaxf(T[0][1], T[0][3]);
+                    #pragma unroll
+                    for (int gi = 1; gi < NG; ++gi) {
+                        mx0 = fmaxf(mx0, fmaxf(T[gi][0], T[gi][2]));
+                        mx1 = fmaxf(mx1, fmaxf(T[gi][1], T[gi][3]));
+                    }
                     #pragma unroll
                     for (int off = 4; off <= 16; off <<= 1) {
                         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
@@ -410,8 +449,7 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
                     const float n0 = fmaxf(M0, fmaf(mx0, us, cz0)), n1 = fmaxf(M1, fmaf(mx1, us, cz1));
                     const float f0 = (M0 == -INFINITY) ? 0.f : fast_exp2(M0 - n0);
                     const float f1 = (M1 == -INFINITY) ? 0.f : fast_exp2(M1 - n1);
-                    const f32x2 ff = f2_pack(f0, f1);
-                    lsum = f2_mul(lsum, ff);
+                    lsum = f2_mul(lsum, f2_pack(f0, f1));
                     #pragma unroll
                     for (int m = 0; m < 6; ++m) {
                         acc[m][0] *= f0; acc[m][1] *= f1; acc[m][2] *= f0; acc[m][3] *= f1;
@@ -421,19 +459,22 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
                     negoff = f2_pack(M0 == -INFINITY ? -INFINITY : cz0 + 12.f - M0,
                                      M1 == -INFINITY ? -INFINITY : cz1 + 12.f - M1);
                 }
-                const float2 e01 = f2_unpack(f2_fma(f2_pack(T[0], T[1]), uu, negoff));
-                const float2 e23 = f2_unpack(f2_fma(f2_pack(T[2], T[3]), uu, negoff));
-                const float p0 = fast_exp2(e01.x), p1 = fast_exp2(e01.y), p2 = fast_exp2(e23.x), p3 = fast_exp2(e23.y);
-                lsum = f2_add(lsum, f2_add(f2_pack(p0, p1), f2_pack(p2, p3)));
-                // hi parts for the columns h < 4, lo parts for the columns h + 4 (no branch: the
-                // transposes below need the whole warp converged)
-                const uint32_t hA = f2h2(p0, p1), hB = f2h2(p2, p3);
-                const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&hA));
-                const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&hB));
-                const uint32_t lA = f2h2(p0 - fa.x, p1 - fa.y), lB = f2h2(p2 - fb.x, p3 - fb.y);
-                const uint32_t wA = (c >= 2) ? lA : hA, wB = (c >= 2) ? lB : hB;
-                pA = movmatrix_t(wA);                           // column g of tokens (c, c + 4)
-                pB = movmatrix_t(wB);                           // column g of tokens (c + 8, c + 12)
+                #pragma unroll
+                for (int gi = 0; gi < NG; ++gi) {
+                    const float2 e01 = f2_unpack(f2_fma(f2_pack(T[gi][0], T[gi][1]), uu, negoff));
+                    const float2 e23 = f2_unpack(f2_fma(f2_pack(T[gi][2], T[gi][3]), uu, negoff));
+                    const float p0 = fast_exp2(e01.x), p1 = fast_exp2(e01.y);
+                    const float p2 = fast_exp2(e23.x), p3 = fast_exp2(e23.y);
+                    lsum = f2_add(lsum, f2_add(f2_pack(p0, p1), f2_pack(p2, p3)));
+                    // hi parts for the columns h < 4, lo parts for the columns h + 4 (no branch:
+                    // the transposes below need the whole warp converged)
+                    const uint32_t hA = f2h2(p0, p1), hB = f2h2(p2, p3);
+                    const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&hA));
+                    const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&hB));
+                    const uint32_t lA = f2h2(p0 - fa.x, p1 - fa.y), lB = f2h2(p2 - fb.x, p3 - fb.y);
+                    pA[gi] = movmatrix_t((c >= 2) ? lA : hA);   // column g of tokens (c, c + 4)
+                    pB[gi] = movmatrix_t((c >= 2) ? lB : hB);   // column g of tokens (c + 8, c + 12)
+                }
             }
             // ---- values: 6 m-tiles (x/y of triplets 4g + m; z of 4g .. 4g + 3) ---------------
             s = slot;
@@ -441,33 +482,41 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
             alive = __all_sync(0xffffffffu, alive);
             if (act && alive) {
                 const uint32_t vb = smem_base + ring_off(s) + wt0 * 64 + v_lane;
-                uint2 vw[4];
+                uint2 vw[NG][4];
                 #pragma unroll
-                for (int t = 0; t < 4; ++t) vw[t] = lds_u32x2m(vb + t * 256);     // tokens c + 4 t
-                const uint32_t d0 = __byte_perm(pA, 0u, 0x1010u), d1 = __byte_perm(pA, 0u, 0x3232u);
-                const uint32_t d2 = __byte_perm(pB, 0u, 0x1010u), d3 = __byte_perm(pB, 0u, 0x3232u);
+                for (int gi = 0; gi < NG; ++gi)
+                    #pragma unroll
+                    for (int t = 0; t < 4; ++t) vw[gi][t] = lds_u32x2m(vb + gi * 1024 + t * 256);   // tokens c + 4 t
                 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
                     const uint32_t sel = (m & 1) ? 0x7624u : 0x7604u;
-                    const uint2 x0 = lds_u32x2m(__byte_perm((m >> 1) ? vw[0].y : vw[0].x, lanereg, sel));
-                    const uint2 x1 = lds_u32x2m(__byte_perm((m >> 1) ? vw[1].y : vw[1].x, lanereg, sel));
-                    const uint2 x2 = lds_u32x2m(__byte_perm((m >> 1) ? vw[2].y : vw[2].x, lanereg, sel));
-                    const uint2 x3 = lds_u32x2m(__byte_perm((m >> 1) ? vw[3].y : vw[3].x, lanereg, sel));
-                    mma16816(acc[m], x0.x, x0.y, x1.x, x1.y, d0, d1);
-                    mma16816(acc[m], x2.x, x2.y, x3.x, x3.y, d2, d3);
+                    #pragma unroll
+                    for (int gi = 0; gi < NG; ++gi) {
+                        const uint32_t d0 = __byte_perm(pA[gi], 0u, 0x1010u), d1 = __byte_perm(pA[gi], 0u, 0x3232u);
+                        const uint32_t d2 = __byte_perm(pB[gi], 0u, 0x1010u), d3 = __byte_perm(pB[gi], 0u, 0x3232u);
+                        const uint2 x0 = lds_u32x2m(__byte_perm((m >> 1) ? vw[gi][0].y : vw[gi][0].x, lanereg, sel));
+                        const uint2 x1 = lds_u32x2m(__byte_perm((m >> 1) ? vw[gi][1].y : vw[gi][1].x, lanereg, sel));
+                        const uint2 x2 = lds_u32x2m(__byte_perm((m >> 1) ? vw[gi][2].y : vw[gi][2].x, lanereg, sel));
+                        const uint2 x3 = lds_u32x2m(__byte_perm((m >> 1) ? vw[gi][3].y : vw[gi][3].x, lanereg, sel));
+                        mma16816(acc[m], x0.x, x0.y, x1.x, x1.y, d0, d1);
+                        mma16816(acc[m], x2.x, x2.y, x3.x, x3.y, d2, d3);
+                    }
                 }
                 #pragma unroll
                 for (int m = 0; m < 2; ++m) {
-                    const uint32_t wa = m ? vw[0].y : vw[0].x, wb = m ? vw[1].y : vw[1].x;
-                    const uint32_t wc2 = m ? vw[2].y : vw[2].x, wd = m ? vw[3].y : vw[3].x;
                     // i_z - 8 of two tokens' codes as exact fp16 (1024 + i_z, less 1032): centred, so
                     // that sum p (i_z - 8) does not grow tile by tile -- o_z = (z0 + 8 dz) l + dz
                     // sum p (i_z - 8) then has no cancellation for the truncating tensor-core sums
                     // to expose.  The tile's sums start from zero and join the running sums by
                     // fp32 adds.
                     float zt[4] = {0.f, 0.f, 0.f, 0.f};
-                    mma16816(zt, zc8(prmt(wa, wb, 0x5511u)), zc8(prmt(wa, wb, 0x7733u)),
-                             zc8(prmt(wc2, wd, 0x5511u)), zc8(prmt(wc2, wd, 0x7733u)), pA, pB);
+                    #pragma unroll
+                    for (int gi = 0; gi < NG; ++gi) {
+                        const uint32_t wa = m ? vw[gi][0].y : vw[gi][0].x, wb = m ? vw[gi][1].y : vw[gi][1].x;
+                        const uint32_t wc2 = m ? vw[gi][2].y : vw[gi][2].x, wd = m ? vw[gi][3].y : vw[gi][3].x;
+                        mma16816(zt, zc8(prmt(wa, wb, 0x5511u)), zc8(prmt(wa, wb, 0x7733u)),
+                                 zc8(prmt(wc2, wd, 0x5511u)), zc8(prmt(wc2, wd, 0x7733u)), pA[gi], pB[gi]);
+                    }
                     #pragma unroll
                     for (int i = 0; i < 4; ++i) acc[4 + m][i] += zt[i];
                 }
@@ -540,7 +589,7 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
             }
         }
         named_bar_sync(1, nthr);
-        finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 1);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, 96, tid, nthr, 1);
     }
     xr_kernel_tail(p, tid, nthr);
 }
