@@ -62,7 +62,7 @@ constexpr int TW = 16 * NG;                             // tokens per warp per t
 constexpr int TT = W * TW;                              // tokens per tile
 constexpr int HALF = TT * 64;                           // K (or V) codes of a tile: 32 x uint16 / token
 constexpr int SLOTS = 4;                                // ring of half tiles
-constexpr int PF = 2;                                   // tiles asked into L2 ahead of the ring
+constexpr int PF = 1;                                   // tiles asked into L2 ahead of the ring
 constexpr int TAB_BYTES = 256 * 32 * 8;                 // [256 flat][32 copies] (x hi|lo, y hi|lo)
 // The dynamic shared window of a kernel without static shared memory starts at shared address
 // 0x400 on sm_100 (the first KB is reserved; checked at run time).  The table must start at a
@@ -85,6 +85,7 @@ static_assert(OFF_QRAW + HQ * 96 * 4 <= OFF_TAB, "slots and queries below the ta
 static_assert(OFF_ACC % 16 == 0 && OFF_BAR % 8 == 0 && HALF % 128 == 0, "alignment");
 static_assert(TOTAL <= 227 * 1024, "one CTA per SM");
 static_assert(W * 32 >= HQ * 96, "one consumer thread per query element (the query prefetch)");
+static_assert((W + 1) * 32 == 2 * 256, "two threads per table row in the fill");
 
 // window offset of ring slot s
 __host__ __device__ constexpr int ring_off(int s) {
@@ -177,7 +178,7 @@ __device__ void produce_g12m(const AttnParams& p, uint8_t* smem, uint64_t* full,
     ItemRange r;
     while (ok && work_next<true>(p, wc, r)) {
         const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.kvh * p.kv_hs) * 2;
-        {
+        if (PF > 0) {
             const uint32_t bytes = (uint32_t)min(PF * TT, r.tok1 - r.tok0) * 64u;
             bulk_prefetch_l2(p.kc + base + (int64_t)r.tok0 * 64, bytes);
             bulk_prefetch_l2(p.vc + base + (int64_t)r.tok0 * 64, bytes);
@@ -185,7 +186,7 @@ __device__ void produce_g12m(const AttnParams& p, uint8_t* smem, uint64_t* full,
         for (int t0 = r.tok0; t0 < r.tok1 && ok; t0 += TT) {
             const uint32_t bytes = (uint32_t)min(TT, r.tok1 - t0) * 64u;
             const int64_t off = base + (int64_t)t0 * 64;
-            if (t0 + PF * TT < r.tok1) {
+            if (PF > 0 && t0 + PF * TT < r.tok1) {
                 const int tp = t0 + PF * TT;
                 const uint32_t pbytes = (uint32_t)min(TT, r.tok1 - tp) * 64u;
                 bulk_prefetch_l2(p.kc + base + (int64_t)tp * 64, pbytes);
@@ -248,12 +249,14 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
     fence_proxy_async_smem();                             // before the bulk copies overwrite it
     // (x, y) table: row e = (i_r << 4) | i_theta, 32 copies of ((x_hi, x_lo), (y_hi, y_lo)) of the
     // codec's decoded (x, y) of the flat index (the uniform polar grid, stacked_plane.py:297-310)
+    // (two threads a row, one load each: the fill costs one L2 round trip)
     {
-        uint2* tab = reinterpret_cast<uint2*>(smem + OFF_TAB);
-        for (int i = tid; i < 256 * 32; i += blockDim.x) {
-            const float2 xy = __ldg(reinterpret_cast<const float2*>(p.dec_xy) + (i >> 5));
-            tab[i] = make_uint2(h2_split(xy.x), h2_split(xy.y));
-        }
+        const int e = tid >> 1, half = tid & 1;
+        const float2 xy = __ldg(reinterpret_cast<const float2*>(p.dec_xy) + e);
+        const uint2 v = make_uint2(h2_split(xy.x), h2_split(xy.y));
+        uint4* row = reinterpret_cast<uint4*>(smem + OFF_TAB + e * 256 + half * 128);
+        #pragma unroll
+        for (int k = 0; k < 8; ++k) row[k] = make_uint4(v.x, v.y, v.x, v.y);
     }
     float qreg = 0.f;                                     // the first item's queries, ahead of the stream
     {
@@ -289,10 +292,19 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
         // q'_h = scale log2(e) R q_h: one warp per row k of R (read through L2), lanes over the
         // input index; the four heads' sums finish in a transpose-reduce, then a butterfly over
         // the low three lane bits
-        #pragma unroll 1
-        for (int k = warp; k < 96; k += W) {
-            const float* row = p.R + k * 96;
-            const float r0 = __ldg(row + lane), r1 = __ldg(row + lane + 32), r2 = __ldg(row + lane + 64);
+        constexpr int RPW = (96 + W - 1) / W;              // rows of R per warp
+        float rr[RPW][3];                                  // all of this warp's rows in flight at once
+        #pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+            const int k = min(warp + i * W, 95);
+            #pragma unroll
+            for (int u = 0; u < 3; ++u) rr[i][u] = __ldg(p.R + k * 96 + lane + 32 * u);
+        }
+        #pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+            const int k = warp + i * W;
+            if (k >= 96) break;
+            const float r0 = rr[i][0], r1 = rr[i][1], r2 = rr[i][2];
             float a[HQ];
             #pragma unroll
             for (int h = 0; h < HQ; ++h)
