@@ -281,7 +281,7 @@ __device__ __forceinline__ void xr_publish(const AttnParams& p, const ItemRange&
 // out rows of the item's unit = (sFin rows) @ R, through store_out.  With parts > 1, up to
 // max_parts threads share an output, each summing a slice of k with two chains; sO (at least
 // max_parts * G * dim floats, dead by now) holds their partial sums.  With one part, each thread
-// batches 16 loads of R ahead of its FMAs.
+// batches 48 loads of R ahead of its FMAs (two L2 round trips for head_dim 96 when R is global).
 __device__ void rotate_out(const AttnParams& p, const ItemRange& r, float* sO, const float* sFin, const float* Rp,
                            int pitch, int tid, int nthr, int max_parts) {
     const int dim = p.dim, greal = p.G;
@@ -292,12 +292,12 @@ __device__ void rotate_out(const AttnParams& p, const ItemRange& r, float* sO, c
         for (int idx = tid; idx < gd; idx += nthr) {
             const int g = idx / dim, i = idx % dim;
             float v = 0.f;
-            for (int k0 = 0; k0 < dim; k0 += 16) {
-                float rv[16];
+            for (int k0 = 0; k0 < dim; k0 += 48) {
+                float rv[48];
                 #pragma unroll
-                for (int u = 0; u < 16; ++u) rv[u] = (k0 + u < dim) ? Rp[(k0 + u) * pitch + i] : 0.f;
+                for (int u = 0; u < 48; ++u) rv[u] = (k0 + u < dim) ? Rp[(k0 + u) * pitch + i] : 0.f;
                 #pragma unroll
-                for (int u = 0; u < 16; ++u)
+                for (int u = 0; u < 48; ++u)
                     if (k0 + u < dim) v = fmaf(sFin[g * dim + k0 + u], rv[u], v);
             }
             store_out(p, r, g, i, v);
@@ -373,6 +373,23 @@ __device__ void xr_arrive(const AttnParams& p, const ItemRange& r, float* sO, fl
     }
 }
 
+// Exchange mode, after the CTA's last item: count the units recorded by finish_item (xr_defer).
+__device__ void xr_flush_deferred(const AttnParams& p, int* xr_defer, float* sO, float* sFin, int* sflag,
+                                  const float* Rp, int pitch, int tid, int nthr, int max_parts) {
+    if (p.xr_world <= 0) return;
+    named_bar_sync(1, nthr);
+    const int n = xr_defer[0];
+    for (int i = 0; i < n; ++i) {
+        const int unit = xr_defer[1 + i];
+        ItemRange r{};
+        r.b = unit / p.Hu;
+        r.hk = unit % p.Hu;
+        xr_arrive(p, r, sO, sFin, sflag, Rp, pitch, tid, nthr, max_parts);
+        named_bar_sync(1, nthr);                      // sO / sFin / sflag free for the next unit
+    }
+    if (tid == 0) xr_defer[0] = 0;
+}
+
 // Exchange mode, once per CTA after its last item: the rank's last CTA waits until every unit's
 // output rows have arrived in this rank's buffer, bounded by xr_wait_ns of device time; on expiry
 // it sets the device error word and leaves the counters as they are (the host resets them).
@@ -402,9 +419,15 @@ __device__ void xr_kernel_tail(const AttnParams& p, int tid, int nthr) {
 // the partial row, or merges splits and writes out = (o / l) @ R, or (exchange mode) publishes
 // the unit's partial rows to every rank and takes part in the cross-rank merge.  All `nthr`
 // consumer threads call it; barrier id 1.
+// xr_defer (exchange mode, optional): a shared list [count, unit...] of XR_DEFER_CAP entries.  With
+// it, a unit whose rows are published is recorded instead of counted at once; xr_flush_deferred at
+// the CTA's end counts them (one system-scope release there, where no copies of the CTA are in
+// flight, instead of a CTA-wide stall on a fence per unit in the middle of the stream).
+constexpr int XR_DEFER_CAP = 15;
+
 __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float* sM, const float* sL,
                             float* sO, float* sFin, int* sflag, const float* Rp, int pitch, int tid,
-                            int nthr, int max_parts) {
+                            int nthr, int max_parts, int* xr_defer = nullptr) {
     const int dim = p.dim, greal = p.G;
     const bool single = (r.nseg == 1);
     const bool xr = p.xr_world > 0;
@@ -472,6 +495,18 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
             }
             finalize = !p.partial_only && !xr;
             arrive = xr;
+        }
+    }
+    if (arrive && xr_defer != nullptr) {
+        named_bar_sync(1, nthr);                      // every thread has read the count below
+        const int n = xr_defer[0];
+        if (n < XR_DEFER_CAP) {
+            named_bar_sync(1, nthr);
+            if (tid == 0) {
+                xr_defer[1 + n] = r.b * p.Hu + r.hk;
+                xr_defer[0] = n + 1;
+            }
+            arrive = false;
         }
     }
     if (arrive) xr_arrive(p, r, sO, sFin, sflag, Rp, pitch, tid, nthr, max_parts);
