@@ -247,23 +247,27 @@ PKV_API int pkv_lse_combine_gather(const pkv_codec *c, const float *const *part_
  * when a unit's (batch row, its query heads) partial softmax state
  * [m (log2 units), l, o_rot[dim]] is final on a rank, the rank stores it into
  * slot `rank` of EVERY rank's exchange buffer (plain peer stores over NVLink),
- * fences, and adds one to the unit's arrival counter at its owner rank
- * (unit % world).  The rank whose addition completes the count merges the
- * world partials (log-sum-exp), applies R once and stores the output rows into
- * every rank's buffer, then counts the unit done at every rank.  The last CTA
- * of each rank's kernel waits -- bounded by wait_limit_us, measured with the
- * device clock -- until all units are done there, then resets its counters.
- * On expiry it sets the device error word to 4 (read by pkv_device_error) and
- * returns; the counters are then left as they were, and every rank must call
- * pkv_xr_reset (after a host-side agreement that the step failed) before the
- * next step.  The buffers are plain cudaMalloc memory (no NVSwitch object)
- * mapped into the peers with CUDA IPC.  The reference has no counterpart: it
- * decodes on one CPU (polar_attention.py:277-309); sharding the sequence is
- * the decomposition of that same softmax.
+ * each value as one 8-byte word (value, flag) whose flag names the call, so
+ * no fences or counters order the exchange.  After its last item every CTA
+ * of every rank merges its share of the units (unit u on CTA u mod grid):
+ * it waits for the flags of all ranks' rows of the unit in its own buffer --
+ * bounded by wait_limit_us, measured with the device clock -- merges them
+ * (log-sum-exp), applies R once and stores the rank's own output rows.  Every
+ * rank computes the same outputs.  The call flag is the rank's call count
+ * (kept in the buffer, advanced by the call's last CTA); the partial slots
+ * alternate with its parity, so a rank one call ahead cannot overwrite rows a
+ * slower rank still reads.  On expiry the device error word is set to 4 (read
+ * by pkv_device_error); every rank must then call pkv_xr_reset (after a
+ * host-side agreement that the step failed) before the next step.  The
+ * buffers are plain cudaMalloc memory (no NVSwitch object) mapped into the
+ * peers with CUDA IPC.  The reference has no counterpart: it decodes on one
+ * CPU (polar_attention.py:277-309); sharding the sequence is the
+ * decomposition of that same softmax.
  *
- * Buffer layout (pkv_xr_layout): partial slots [world][rows][dim + 2] f32,
- * output rows [rows][dim] f32 (rows = batch * q_heads, row b * q_heads + h),
- * unit counters, a done counter and a CTA counter; zero when allocated.      */
+ * Buffer layout (pkv_xr_layout): partial slots [2][world][rows][dim + 2] of
+ * 8-byte (f32 value, u32 flag) words, output rows [rows][dim] f32 (rows =
+ * batch * q_heads, row b * q_heads + h), two control words (call count, CTA
+ * count); zero when allocated.                                              */
 #define PKV_XR_MAX_RANKS 8
 typedef struct pkv_exchange {
     int32_t world, rank;
@@ -283,10 +287,11 @@ PKV_API int pkv_xr_alloc(uint64_t bytes, void **dev_ptr, void *ipc_handle_out);
 PKV_API int pkv_xr_open(const void *ipc_handle, void **dev_ptr);
 PKV_API int pkv_xr_close(void *peer_ptr);
 PKV_API int pkv_xr_free(void *dev_ptr);
-/* Zero this rank's counters (after an expired wait; every rank, between steps). */
+/* Zero this rank's buffer, call count included (after an expired wait; every
+ * rank, between steps).                                                      */
 PKV_API int pkv_xr_reset(const pkv_codec *c, const pkv_attn_args *a, const pkv_exchange *x, void *stream);
-/* a->partial_only must be 0 and a->out is unused: outputs land in every rank's
- * buffer at out_offset.  a->seq_len is this rank's shard length; batch, heads
+/* a->partial_only must be 0 and a->out is unused: outputs land in this rank's
+ * buffer at out_offset (every rank merges its own copy).  a->seq_len is this rank's shard length; batch, heads
  * and the plan's unit decomposition must agree across ranks.                  */
 PKV_API int pkv_attn_decode_xr(const pkv_codec *c, const pkv_attn_args *a, void *workspace, size_t workspace_bytes,
                                const pkv_exchange *x, void *stream);

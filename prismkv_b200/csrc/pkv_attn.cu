@@ -79,7 +79,7 @@ struct AttnParams {
     // units every rank counts, and the bound on the completion wait
     int xr_world, xr_rank, xr_units;
     uint8_t* xr_buf[PKV_XR_MAX_RANKS];
-    int64_t xr_out_off, xr_cnt_off, xr_done_off;
+    int64_t xr_out_off, xr_ctl_off;
     uint64_t xr_wait_ns;
 };
 
@@ -232,23 +232,21 @@ __device__ __forceinline__ void rotate_query(const AttnParams& p, const ItemRang
 }
 
 // ---------------------------------------------------------------------------
-// split-sequence exchange primitives (system scope: the peers are other GPUs)
+// split-sequence exchange (the peers are other GPUs, reached through CUDA-IPC peer memory).
+// Protocol with the flag in the word: every partial value travels as one 8-byte store of (value,
+// flag), flag = epoch + 1, and a naturally aligned 8-byte access is single-copy atomic, so a
+// reader that sees the flag sees the value -- no fences, no counters.  The epoch counts this
+// rank's calls (advanced by the call's last CTA); the slots alternate by its parity, so a rank one
+// call ahead never overwrites what a slower rank still reads (it cannot get two calls ahead: its
+// next call needs the slower rank's partials of that call).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t* ptr, uint32_t v) {
-    uint32_t old;
-    asm volatile("atom.add.acq_rel.sys.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
-    return old;
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* ptr, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(ptr), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ void red_add_release_sys(uint32_t* ptr, uint32_t v) {
-    asm volatile("red.add.release.sys.global.u32 [%0], %1;" :: "l"(ptr), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* ptr) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
     return v;
 }
 
@@ -258,24 +256,53 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
+// This call's epoch (control word 0 of this rank's buffer; it changes only after every CTA of
+// the call is done).
+__device__ __forceinline__ uint32_t xr_epoch(const AttnParams& p) {
+    return *reinterpret_cast<const volatile uint32_t*>(p.xr_buf[p.xr_rank] + p.xr_ctl_off);
+}
+
+// Word k of the partial row `row` from rank `src` in rank `dst`'s buffer, slot parity `par`.
+__device__ __forceinline__ uint64_t* xr_word(const AttnParams& p, int dst, uint32_t par, int src, int64_t row, int k) {
+    return reinterpret_cast<uint64_t*>(p.xr_buf[dst]) +
+           ((((int64_t)par * p.xr_world + src) * p.B * p.Hq + row) * (p.dim + 2) + k);
+}
+
 // Output element (query head g of the item's unit, dim i): the caller's output, or in exchange
-// mode the output rows of every rank's buffer.
+// mode this rank's output rows (every rank merges its own copy).
 __device__ __forceinline__ void store_out(const AttnParams& p, const ItemRange& r, int g, int i, float v) {
     const int hq = r.hk * p.G + g;
     if (p.xr_world > 0) {
         const int64_t off = p.xr_out_off + (((int64_t)r.b * p.Hq + hq) * p.dim + i) * 4;
-        for (int s = 0; s < p.xr_world; ++s) *reinterpret_cast<float*>(p.xr_buf[s] + off) = v;
+        *reinterpret_cast<float*>(p.xr_buf[p.xr_rank] + off) = v;
     } else {
         p.out[(int64_t)r.b * p.out_bs + (int64_t)hq * p.out_hs + i] = v;
     }
 }
 
 // Exchange mode: element k of this rank's final partial row of query head g ([m (log2 units), l,
-// o_rot]) into slot xr_rank of every rank's buffer.
-__device__ __forceinline__ void xr_publish(const AttnParams& p, const ItemRange& r, int g, int k, float val) {
+// o_rot]) into slot xr_rank of every rank's buffer, flagged with this call's epoch.
+__device__ __forceinline__ void xr_publish(const AttnParams& p, const ItemRange& r, int g, int k, float val,
+                                           uint32_t epoch) {
     const int64_t row = (int64_t)r.b * p.Hq + r.hk * p.G + g;
-    const int64_t off = (((int64_t)p.xr_rank * p.B * p.Hq + row) * (p.dim + 2) + k) * 4;
-    for (int s = 0; s < p.xr_world; ++s) *reinterpret_cast<float*>(p.xr_buf[s] + off) = val;
+    const uint64_t w = ((uint64_t)(epoch + 1u) << 32) | (uint64_t)__float_as_uint(val);
+    for (int s = 0; s < p.xr_world; ++s) st_relaxed_sys_u64(xr_word(p, s, epoch & 1u, p.xr_rank, row, k), w);
+}
+
+// The value of a flagged word once its flag is this call's, bounded by xr_wait_ns from t0 (or
+// given up at once when the device error word is already set); on expiry the error word is set
+// and 0 returned.
+__device__ __forceinline__ float xr_take(const uint64_t* ptr, uint32_t flag, uint64_t t0, uint64_t limit) {
+    for (;;) {
+        const uint64_t w = ld_relaxed_sys_u64(ptr);
+        if ((uint32_t)(w >> 32) == flag) return __uint_as_float((uint32_t)w);
+        if (*reinterpret_cast<volatile int32_t*>(&g_device_error) != 0) return 0.f;
+        if (global_ns() - t0 > limit) {
+            flag_error(kErrPeerWait);
+            return 0.f;
+        }
+        __nanosleep(64);
+    }
 }
 
 // out rows of the item's unit = (sFin rows) @ R, through store_out.  With parts > 1, up to
@@ -327,90 +354,62 @@ __device__ void rotate_out(const AttnParams& p, const ItemRange& r, float* sO, c
     }
 }
 
-// Exchange mode, after this rank's partial rows of the unit are in every rank's buffer: count
-// the arrival at the unit's owner rank; the rank that completes the count merges the world
-// partials from its own buffer (every rank stored into every buffer before counting), applies R
-// once, stores the rows into every rank's output and counts the unit done at every rank.
-__device__ void xr_arrive(const AttnParams& p, const ItemRange& r, float* sO, float* sFin, int* sflag,
-                          const float* Rp, int pitch, int tid, int nthr, int max_parts) {
+// Exchange mode: wait for every rank's partial rows of the unit in this rank's buffer (flag =
+// this call's epoch + 1), merge them (log-sum-exp), apply R once and store this rank's output rows.
+__device__ void xr_merge_unit(const AttnParams& p, const ItemRange& r, float* sO, float* sFin, const float* Rp,
+                              int pitch, int tid, int nthr, int max_parts) {
     const int dim = p.dim, greal = p.G;
-    // the CTA's peer stores are ordered before thread 0's system-scope release by the barrier
-    // (causality is transitive through bar.sync): one fence for the CTA, not one per thread
     named_bar_sync(1, nthr);
-    if (tid == 0) {
-        fence_acq_rel_sys();
-        const int unit = r.b * p.Hu + r.hk;
-        uint32_t* cnt = reinterpret_cast<uint32_t*>(p.xr_buf[unit % p.xr_world] + p.xr_cnt_off) + unit;
-        const uint32_t old = atom_add_acq_rel_sys(cnt, 1u);
-        const int last = (old == (uint32_t)p.xr_world - 1);
-        if (last) *reinterpret_cast<volatile uint32_t*>(cnt) = 0u;     // the next step counts from zero
-        sflag[0] = last;
-    }
-    named_bar_sync(1, nthr);
-    if (!sflag[0]) return;
-    const float* part = reinterpret_cast<const float*>(p.xr_buf[p.xr_rank]);
-    const int64_t slot = (int64_t)p.B * p.Hq * (dim + 2);
+    const uint32_t epoch = xr_epoch(p), flag = epoch + 1u, par = epoch & 1u;
+    const uint64_t t0 = global_ns();
     for (int idx = tid; idx < greal * dim; idx += nthr) {
         const int g = idx / dim, k = idx % dim;
-        const float* src = part + ((int64_t)r.b * p.Hq + r.hk * greal + g) * (dim + 2);
+        const int64_t row = (int64_t)r.b * p.Hq + r.hk * greal + g;
+        float ms[PKV_XR_MAX_RANKS], ls[PKV_XR_MAX_RANKS], os[PKV_XR_MAX_RANKS];
         float M = -INFINITY;
-        for (int s = 0; s < p.xr_world; ++s) M = fmaxf(M, __ldcg(src + s * slot));
+        #pragma unroll
+        for (int s = 0; s < PKV_XR_MAX_RANKS; ++s) {
+            if (s >= p.xr_world) break;
+            ms[s] = xr_take(xr_word(p, p.xr_rank, par, s, row, 0), flag, t0, p.xr_wait_ns);
+            ls[s] = xr_take(xr_word(p, p.xr_rank, par, s, row, 1), flag, t0, p.xr_wait_ns);
+            os[s] = xr_take(xr_word(p, p.xr_rank, par, s, row, 2 + k), flag, t0, p.xr_wait_ns);
+            M = fmaxf(M, ms[s]);
+        }
         float v = 0.f, l = 0.f;
-        for (int s = 0; s < p.xr_world; ++s) {
-            const float ms = __ldcg(src + s * slot);
-            const float f = (ms == -INFINITY) ? 0.f : fast_exp2(ms - M);
-            l = fmaf(__ldcg(src + s * slot + 1), f, l);
-            v = fmaf(__ldcg(src + s * slot + 2 + k), f, v);
+        #pragma unroll
+        for (int s = 0; s < PKV_XR_MAX_RANKS; ++s) {
+            if (s >= p.xr_world) break;
+            const float f = (ms[s] == -INFINITY) ? 0.f : fast_exp2(ms[s] - M);
+            l = fmaf(ls[s], f, l);
+            v = fmaf(os[s], f, v);
         }
         sFin[g * dim + k] = (l > 0.f) ? v / l : 0.f;
     }
     rotate_out(p, r, sO, sFin, Rp, pitch, tid, nthr, max_parts);
-    named_bar_sync(1, nthr);
-    if (tid == 0) {
-        fence_acq_rel_sys();
-        for (int s = 0; s < p.xr_world; ++s)
-            red_add_release_sys(reinterpret_cast<uint32_t*>(p.xr_buf[s] + p.xr_done_off), 1u);
-    }
 }
 
-// Exchange mode, after the CTA's last item: count the units recorded by finish_item (xr_defer).
-__device__ void xr_flush_deferred(const AttnParams& p, int* xr_defer, float* sO, float* sFin, int* sflag,
-                                  const float* Rp, int pitch, int tid, int nthr, int max_parts) {
+// Exchange mode, once per CTA after its last item (every kernel's tail): merge the units assigned
+// to this CTA (u = blockIdx.x, + gridDim.x, ...) into this rank's output rows; then the call's
+// last CTA advances the epoch (every CTA has merged its units by then; the next call, stream-
+// ordered, reads the new epoch).  A CTA waits for partials only after it has published all of its
+// own, so no two CTAs of any ranks can wait on each other.  sO / sFin / R as for finish_item.
+__device__ void xr_finish_call(const AttnParams& p, float* sO, float* sFin, const float* Rp, int pitch, int tid,
+                               int nthr, int max_parts) {
     if (p.xr_world <= 0) return;
-    named_bar_sync(1, nthr);
-    const int n = xr_defer[0];
-    for (int i = 0; i < n; ++i) {
-        const int unit = xr_defer[1 + i];
+    for (int u = blockIdx.x; u < p.xr_units; u += gridDim.x) {
         ItemRange r{};
-        r.b = unit / p.Hu;
-        r.hk = unit % p.Hu;
-        xr_arrive(p, r, sO, sFin, sflag, Rp, pitch, tid, nthr, max_parts);
-        named_bar_sync(1, nthr);                      // sO / sFin / sflag free for the next unit
+        r.b = u / p.Hu;
+        r.hk = u % p.Hu;
+        xr_merge_unit(p, r, sO, sFin, Rp, pitch, tid, nthr, max_parts);
+        named_bar_sync(1, nthr);                      // sO / sFin free for the next unit
     }
-    if (tid == 0) xr_defer[0] = 0;
-}
-
-// Exchange mode, once per CTA after its last item: the rank's last CTA waits until every unit's
-// output rows have arrived in this rank's buffer, bounded by xr_wait_ns of device time; on expiry
-// it sets the device error word and leaves the counters as they are (the host resets them).
-__device__ void xr_kernel_tail(const AttnParams& p, int tid, int nthr) {
-    if (p.xr_world <= 0) return;
     named_bar_sync(1, nthr);
     if (tid != 0) return;
-    uint32_t* done = reinterpret_cast<uint32_t*>(p.xr_buf[p.xr_rank] + p.xr_done_off);
-    uint32_t* ctas = done + 1;
+    uint32_t* ctl = reinterpret_cast<uint32_t*>(p.xr_buf[p.xr_rank] + p.xr_ctl_off);
     __threadfence();
-    if (atomicAdd(ctas, 1u) != gridDim.x - 1) return;
-    const uint64_t t0 = global_ns();
-    while (ld_acquire_sys(done) < (uint32_t)p.xr_units) {
-        if (global_ns() - t0 > p.xr_wait_ns) {
-            flag_error(kErrPeerWait);
-            return;
-        }
-        __nanosleep(200);
-    }
-    *reinterpret_cast<volatile uint32_t*>(done) = 0u;
-    *reinterpret_cast<volatile uint32_t*>(ctas) = 0u;
+    if (atomicAdd(ctl + 1, 1u) != gridDim.x - 1) return;
+    *reinterpret_cast<volatile uint32_t*>(ctl + 1) = 0u;
+    *reinterpret_cast<volatile uint32_t*>(ctl) = ctl[0] + 1u;
     __threadfence();
 }
 
@@ -419,18 +418,13 @@ __device__ void xr_kernel_tail(const AttnParams& p, int tid, int nthr) {
 // the partial row, or merges splits and writes out = (o / l) @ R, or (exchange mode) publishes
 // the unit's partial rows to every rank and takes part in the cross-rank merge.  All `nthr`
 // consumer threads call it; barrier id 1.
-// xr_defer (exchange mode, optional): a shared list [count, unit...] of XR_DEFER_CAP entries.  With
-// it, a unit whose rows are published is recorded instead of counted at once; xr_flush_deferred at
-// the CTA's end counts them (one system-scope release there, where no copies of the CTA are in
-// flight, instead of a CTA-wide stall on a fence per unit in the middle of the stream).
-constexpr int XR_DEFER_CAP = 15;
-
 __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float* sM, const float* sL,
                             float* sO, float* sFin, int* sflag, const float* Rp, int pitch, int tid,
-                            int nthr, int max_parts, int* xr_defer = nullptr) {
+                            int nthr, int max_parts) {
     const int dim = p.dim, greal = p.G;
     const bool single = (r.nseg == 1);
     const bool xr = p.xr_world > 0;
+    const uint32_t epoch = xr ? xr_epoch(p) : 0u;
     bool finalize = single && !p.partial_only && !xr;
     bool arrive = single && xr;
     for (int idx = tid; idx < greal * (dim + 2); idx += nthr) {
@@ -445,7 +439,7 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
                 float* dst = p.ws_part + (((int64_t)r.b * p.Hq + hq) * p.slots + r.split) * (dim + 2);
                 dst[k] = val;
             } else if (xr) {
-                xr_publish(p, r, g, k, val);
+                xr_publish(p, r, g, k, val, epoch);
             } else {
                 float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
                 dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : val;
@@ -478,7 +472,7 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
                     if (k >= 2) v = fmaf(__ldcg(src + sp * (dim + 2) + k), f, v);
                 }
                 if (xr) {
-                    xr_publish(p, r, g, k, (k == 0) ? M : (k == 1 ? lsw : v));
+                    xr_publish(p, r, g, k, (k == 0) ? M : (k == 1 ? lsw : v), epoch);
                 } else if (p.partial_only) {
                     float* dst = p.partial_out + ((int64_t)r.b * p.Hq + hq) * (dim + 2);
                     dst[k] = (k == 0) ? (M == -INFINITY ? -INFINITY : M * kLn2) : (k == 1 ? lsw : v);
@@ -497,19 +491,7 @@ __device__ void finish_item(const AttnParams& p, const ItemRange& r, const float
             arrive = xr;
         }
     }
-    if (arrive && xr_defer != nullptr) {
-        named_bar_sync(1, nthr);                      // every thread has read the count below
-        const int n = xr_defer[0];
-        if (n < XR_DEFER_CAP) {
-            named_bar_sync(1, nthr);
-            if (tid == 0) {
-                xr_defer[1 + n] = r.b * p.Hu + r.hk;
-                xr_defer[0] = n + 1;
-            }
-            arrive = false;
-        }
-    }
-    if (arrive) xr_arrive(p, r, sO, sFin, sflag, Rp, pitch, tid, nthr, max_parts);
+    (void)arrive;                                     // exchange: merged at the CTA's end (xr_finish_call)
     if (finalize) rotate_out(p, r, sO, sFin, Rp, pitch, tid, nthr, max_parts);
     // the next item may overwrite sFin / sO / sflag only after every thread is done with them
     named_bar_sync(1, nthr);
@@ -816,7 +798,7 @@ __global__ void __launch_bounds__(kPW * 32 + 32, 2) attn_polar_kernel(AttnParams
         named_bar_sync(1, nthr);
         finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, dim, tid, nthr, 4);
     }
-    xr_kernel_tail(p, tid, nthr);
+    xr_finish_call(p, sAcc, sFin, p.R, dim, tid, nthr, 4);
 }
 
 // ---------------------------------------------------------------------------
@@ -1104,7 +1086,7 @@ __global__ void __launch_bounds__(TMA ? kLW * 32 + 32 : kLW * 32) attn_lut_kerne
         named_bar_sync(1, nthr);
         finish_item(p, r, sM, sL, sO, sFin, sflag, sR, pitch, tid, nthr, 1);
     }
-    xr_kernel_tail(p, tid, nthr);
+    xr_finish_call(p, sO, sFin, sR, pitch, tid, nthr, 1);
 }
 
 // ---------------------------------------------------------------------------
@@ -1491,17 +1473,18 @@ static int launch_lut(const AttnParams& p, const AttnPlan& pl, cudaStream_t st) 
 
 // Split-sequence exchange buffer of one rank: partial slots [world][rows][dim + 2], output rows
 // [rows][dim], one arrival counter per unit, then the done and CTA counters; 256-byte aligned parts.
-struct XrLayout { size_t out_off, cnt_off, done_off, bytes; int rows, units; };
+// Exchange buffer of a rank: partial slots [2 parities][world][rows][dim + 2] of flagged 8-byte
+// words, output rows [rows][dim] f32, control words (epoch, CTA count).
+struct XrLayout { size_t out_off, ctl_off, bytes; int rows, units; };
 
 static XrLayout xr_layout_of(const pkv_codec* c, const pkv_attn_args* a, const AttnPlan& pl, int world) {
     auto up = [](size_t x) { return (x + 255) / 256 * 256; };
     XrLayout L{};
     L.rows = a->batch * a->q_heads;
     L.units = a->batch * units_per_row(pl, a);
-    L.out_off = up((size_t)world * L.rows * (c->dim + 2) * sizeof(float));
-    L.cnt_off = L.out_off + up((size_t)L.rows * c->dim * sizeof(float));
-    L.done_off = L.cnt_off + up((size_t)L.units * sizeof(uint32_t));
-    L.bytes = L.done_off + 256;
+    L.out_off = up((size_t)2 * world * L.rows * (c->dim + 2) * sizeof(uint64_t));
+    L.ctl_off = L.out_off + up((size_t)L.rows * c->dim * sizeof(float));
+    L.bytes = L.ctl_off + 256;
     return L;
 }
 
@@ -1513,11 +1496,12 @@ void xr_layout(const pkv_codec* c, const pkv_attn_args* a, int world, pkv_xr_lay
     out->units = L.units;
 }
 
-// Byte offset and length of a rank's counters (the part pkv_xr_reset zeroes).
+// Byte offset and length of what pkv_xr_reset zeroes: the whole buffer (slots, whose stale flags
+// must not match the restarted epochs, outputs and control words).
 void xr_counter_span(const pkv_codec* c, const pkv_attn_args* a, int world, size_t* off, size_t* len) {
     const XrLayout L = xr_layout_of(c, a, plan_attn(c, a), world);
-    *off = L.cnt_off;
-    *len = L.bytes - L.cnt_off;
+    *off = 0;
+    *len = L.bytes;
 }
 
 int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_bytes, cudaStream_t st,
@@ -1567,11 +1551,18 @@ int launch_attn(const pkv_codec* c, const pkv_attn_args* a, void* ws, size_t ws_
         p.xr_units = L.units;
         for (int s = 0; s < xr->world; ++s) p.xr_buf[s] = static_cast<uint8_t*>(xr->buffers[s]);
         p.xr_out_off = (int64_t)L.out_off;
-        p.xr_cnt_off = (int64_t)L.cnt_off;
-        p.xr_done_off = (int64_t)L.done_off;
+        p.xr_ctl_off = (int64_t)L.ctl_off;
         p.xr_wait_ns = (uint64_t)xr->wait_limit_us * 1000ull;
         p.partial_only = 0;
         p.out = nullptr;
+        if (p.num_items == 0) {
+            // an empty shard still publishes an empty partial (m = -inf, l = 0) for every unit
+            // and merges its outputs: one empty item per unit
+            p.bal = 0;
+            p.nsplit = 1;
+            p.chunk = 1;
+            p.num_items = a->batch * p.Hu;
+        }
     }
     if (p.num_items == 0) return PKV_OK;
     if (pl.tc) {

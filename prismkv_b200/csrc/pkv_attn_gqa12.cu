@@ -479,7 +479,7 @@ __global__ void __launch_bounds__(gqa12::W * 32 + 32, 1) attn_gqa12_kernel(AttnP
         named_bar_sync(1, nthr);
         finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 1);
     }
-    xr_kernel_tail(p, tid, nthr);
+    xr_finish_call(p, sAcc, sFin, sR, 96, tid, nthr, 1);
 }
 
 }  // namespace pkv

@@ -78,8 +78,7 @@ constexpr int OFF_ACC = OFF_TAB + TAB_BYTES;            // item merge [W][4][96]
 constexpr int OFF_WML = OFF_ACC + W * HQ * 96 * 4;      // [W][4] max, [W][4] sum
 constexpr int OFF_FIN = OFF_WML + 2 * W * HQ * 4;       // [4][96]
 constexpr int OFF_MISC = OFF_FIN + HQ * 96 * 4;         // sM[4], sL[4], sC[4], flag, amax[W]
-constexpr int OFF_DEFER = OFF_MISC + 128;               // exchange: units awaiting their count
-constexpr int OFF_BAR = OFF_DEFER + 64;                 // full[SLOTS], empty[SLOTS]
+constexpr int OFF_BAR = OFF_MISC + 128;                 // full[SLOTS], empty[SLOTS]
 constexpr int OFF_RING_HI = (OFF_BAR + 2 * SLOTS * 8 + 127) / 128 * 128;
 constexpr int TOTAL = OFF_RING_HI + (SLOTS - SLOTS_LO) * HALF;
 static_assert(OFF_QRAW + HQ * 96 * 4 <= OFF_TAB, "slots and queries below the table");
@@ -179,7 +178,7 @@ __device__ void produce_g12m(const AttnParams& p, uint8_t* smem, uint64_t* full,
     ItemRange r;
     while (ok && work_next<true>(p, wc, r)) {
         const int64_t base = ((int64_t)r.b * p.kv_bs + (int64_t)r.kvh * p.kv_hs) * 2;
-        if (PF > 0) {
+        if (PF > 0 && r.tok1 > r.tok0) {                  // (ragged rows leave items empty or inverted)
             const uint32_t bytes = (uint32_t)min(PF * TT, r.tok1 - r.tok0) * 64u;
             bulk_prefetch_l2(p.kc + base + (int64_t)r.tok0 * 64, bytes);
             bulk_prefetch_l2(p.vc + base + (int64_t)r.tok0 * 64, bytes);
@@ -223,7 +222,6 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
     float* sC = sM + 8;
     int* sflag = reinterpret_cast<int*>(sM + 12);
     float* sAmax = sM + 16;                               // [W]
-    int* sDefer = reinterpret_cast<int*>(smem + OFF_DEFER);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + SLOTS;
 
@@ -242,7 +240,6 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
             mbar_init(&empty[s], W);
         }
         fence_mbar_init();
-        sDefer[0] = 0;
     }
     // the ring starts zeroed, so a partial tile's tail never holds bytes that decode to NaN
     for (int i = tid; i < SLOTS * HALF / 16; i += blockDim.x) {
@@ -604,10 +601,9 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
             }
         }
         named_bar_sync(1, nthr);
-        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, 96, tid, nthr, 1, sDefer);
+        finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, 96, tid, nthr, 1);
     }
-    xr_flush_deferred(p, sDefer, sAcc, sFin, sflag, p.R, 96, tid, nthr, 1);
-    xr_kernel_tail(p, tid, nthr);
+    xr_finish_call(p, sAcc, sFin, p.R, 96, tid, nthr, 1);
 }
 
 }  // namespace pkv

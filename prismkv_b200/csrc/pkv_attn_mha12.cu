@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(mha12::W * 32 + 32, 2) attn_mha12_kernel(AttnP
         named_bar_sync(1, nthr);
         finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 1);
     }
-    xr_kernel_tail(p, tid, nthr);
+    xr_finish_call(p, sAcc, sFin, sR, 96, tid, nthr, 1);
     // the last R copy must land before the CTA exits
     if (tid == 0 && alive) mbar_wait(rbar, ruse & 1, kErrWaitDrain);
 }
@@ -607,7 +607,7 @@ __global__ void __launch_bounds__(mha12s::W * 32 + 32, 2) attn_mha12_stream_kern
         named_bar_sync(1, nthr);
         finish_item(p, r, sM, sL, sAcc, sFin, sflag, p.R, 96, tid, nthr, 4);
     }
-    xr_kernel_tail(p, tid, nthr);
+    xr_finish_call(p, sAcc, sFin, p.R, 96, tid, nthr, 4);
 }
 
 }  // namespace pkv

@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(mha8::W * 32 + 32, 1) attn_mha8_kernel(AttnPar
         named_bar_sync(1, nthr);
         finish_item(p, r, sM, sL, sAcc, sFin, sflag, sR, 96, tid, nthr, 4);
     }
-    xr_kernel_tail(p, tid, nthr);
+    xr_finish_call(p, sAcc, sFin, sR, 96, tid, nthr, 4);
     // a copy of R that never landed must not outlive the CTA
     if (tid == 0 && !alive) mbar_wait(rbar, 0, kErrWaitDrain);
 }

@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(atc::threads_for(GM), 1) attn_tc_kernel(AttnPa
             named_bar_sync(1, nthr);
             finish_item(p, r, sM, sL, sO, sFin, sflag, p.R, D, gt, nthr, 1);
         }
-        xr_kernel_tail(p, gt, nthr);
+        xr_finish_call(p, sO, sFin, p.R, D, gt, nthr, 1);
     }
     etc::tc_fence_before();
     __syncthreads();

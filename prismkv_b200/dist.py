@@ -9,10 +9,11 @@ Two partitionings of the decode-attention path:
   (batch, q head).  Either one NCCL all-gather exchanges them (4 B x
   (dim + 2) per row and rank) and ``pkv_lse_combine`` merges them, or
   (``SequenceExchange``, the fast path) the attention kernel itself stores
-  each finished unit's partial rows into every rank's CUDA-IPC-mapped buffer,
-  counts them at the unit's owner rank with a system-scope atomic, and the
-  rank that completes the count merges and applies ``R`` -- one launch per
-  step, every cross-GPU wait bounded.  The merge is the log-sum-exp rule
+  each finished unit's partial rows into every rank's CUDA-IPC-mapped buffer
+  as flagged 8-byte words, and after its last item every CTA of every rank
+  waits for the flags of its share of the units, merges them and applies
+  ``R`` -- one launch per step, no fences or counters, every cross-GPU wait
+  bounded.  The merge is the log-sum-exp rule
   ``o = sum_i e^(m_i - M) o_i / sum_i e^(m_i - M) l_i``.
 * **Batch shards.**  Rank r holds batch rows ``shard_range(B, N, r)``; the
   ranks share nothing and no collective runs.
@@ -74,9 +75,9 @@ class SequenceExchange:
     bound to any NVSwitch object) and exports its CUDA IPC handle; the handles are all-gathered over the process group
     and every rank maps every peer's buffer (pkv_xr_open, plain peer memory over NVLink).  A
     decode step is then ONE kernel launch per rank: the kernel stores each finished unit's
-    partial rows into every rank's buffer, counts its arrival at the unit's owner rank, and the
-    rank that completes a count merges the world partials, applies R and stores the output rows
-    into every rank's buffer.  ``out`` is this rank's copy of those rows, (B, Hq, dim) fp32; a
+    partial rows into every rank's buffer as (value, call flag) words, and every rank merges
+    the world partials of each unit in its own buffer once their flags are in, applies R and
+    stores its output rows.  ``out`` is this rank's copy of those rows, (B, Hq, dim) fp32; a
     step overwrites it, so read it before the next step.  Every cross-rank wait is bounded by
     ``wait_ms`` of device time; after an expiry (``check`` raises) every rank must ``reset``.
 
@@ -84,7 +85,7 @@ class SequenceExchange:
     query dtype); later calls must have the same shapes apart from the token count.
     ``SequenceExchange.single_process`` builds ``world`` buffers on one device with this process
     as rank 0 -- world 1 runs the whole protocol on one GPU; with world > 1 nothing plays the
-    other ranks, so the completion wait runs out (a test of the bounded wait).
+    other ranks, so the wait for their partials runs out (a test of the bounded wait).
     """
 
     def __init__(self, quantizer, q: torch.Tensor, k_codes: torch.Tensor, group=None, wait_ms: float = 1000.0,

@@ -1,12 +1,12 @@
 """The in-kernel split-sequence exchange (pkv_attn_decode_xr) on one GPU.
 
-With one rank the whole protocol runs -- partial rows stored into the exchange buffer, the
-arrival count at the owner, the merge, R, the output rows, the done count and the bounded
-completion wait -- and must give the unsplit kernel's output, call after call (the counters
-reset themselves).  With two ranks in one process nothing plays the second rank: no unit's count
-completes, so the completion wait must run out after its short bound, set the device error word
-(4) and return; after pkv_xr_reset the exchange works again.  No second kernel is involved in
-either case: the wait that runs out waits on a counter that nothing increments.
+With one rank the whole protocol runs -- partial rows stored into the exchange buffer as
+flagged words, every CTA's share of the units merged once their flags are in, R, the output
+rows, the call count advanced -- and must give the unsplit kernel's output, call after call (the
+flags of one call never match the next's).  With two ranks in one process nothing plays the
+second rank: its partials never arrive, so the merge's wait must run out after its short bound,
+set the device error word (4) and return; after pkv_xr_reset the exchange works again.  No
+second kernel is involved in either case: the wait that runs out waits on words nothing writes.
 """
 
 import numpy as np
