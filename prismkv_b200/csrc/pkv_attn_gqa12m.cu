@@ -241,12 +241,21 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
         }
         fence_mbar_init();
     }
-    // the ring starts zeroed, so a partial tile's tail never holds bytes that decode to NaN
-    for (int i = tid; i < SLOTS * HALF / 16; i += blockDim.x) {
-        const int sl = i / (HALF / 16), o = i % (HALF / 16);
-        reinterpret_cast<uint4*>(smem + ring_off(sl))[o] = make_uint4(0u, 0u, 0u, 0u);
+    // A partial tile's tail in the ring holds stale or never-written bytes; every decode of a code
+    // byte is finite whatever it holds (table rows, masked z nibbles, z bytes as small fp16
+    // subnormals), and tokens past the end get score -inf and weight 0, so the ring needs no
+    // clearing.
+    //
+    // The CTA's first global loads in flight at once: the first item's queries, the decode grid
+    // for the table, and R asked into L2 for the first query rotation.
+    float qreg = 0.f;
+    {
+        WorkCursor pc = work_begin(p);
+        ItemRange r0;
+        if (tid < HQ * 96 && work_next<true>(p, pc, r0))
+            qreg = q_load(p.q, p.qdt, (int64_t)r0.b * p.q_bs + (int64_t)(r0.hk * HQ + tid / 96) * p.q_hs + tid % 96);
     }
-    fence_proxy_async_smem();                             // before the bulk copies overwrite it
+    if (tid < 96 * 96 * 4 / 128) prefetch_l2(reinterpret_cast<const uint8_t*>(p.R) + tid * 128);
     // (x, y) table: row e = (i_r << 4) | i_theta, 32 copies of ((x_hi, x_lo), (y_hi, y_lo)) of the
     // codec's decoded (x, y) of the flat index (the uniform polar grid, stacked_plane.py:297-310)
     // (two threads a row, one load each: the fill costs one L2 round trip)
@@ -257,13 +266,6 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
         uint4* row = reinterpret_cast<uint4*>(smem + OFF_TAB + e * 256 + half * 128);
         #pragma unroll
         for (int k = 0; k < 8; ++k) row[k] = make_uint4(v.x, v.y, v.x, v.y);
-    }
-    float qreg = 0.f;                                     // the first item's queries, ahead of the stream
-    {
-        WorkCursor pc = work_begin(p);
-        ItemRange r0;
-        if (tid < HQ * 96 && work_next<true>(p, pc, r0))
-            qreg = q_load(p.q, p.qdt, (int64_t)r0.b * p.q_bs + (int64_t)(r0.hk * HQ + tid / 96) * p.q_hs + tid % 96);
     }
     __syncthreads();
     if (warp == W) {
