@@ -289,19 +289,20 @@ __global__ void __launch_bounds__(g12m::W * 32 + 32, 1) attn_gqa12_mma_kernel(At
     while (work_next<true>(p, wc, r)) {
         const int ntok = r.tok1 - r.tok0;
         const int ntiles = (ntok + TT - 1) / TT;
-        if (tid < HQ * 96) sQraw[tid] = qreg;
-        named_bar_sync(1, nthr);
-        // q'_h = scale log2(e) R q_h: one warp per row k of R (read through L2), lanes over the
-        // input index; the four heads' sums finish in a transpose-reduce, then a butterfly over
-        // the low three lane bits
+        // q'_h = scale log2(e) R q_h: one warp per row k of R (read through L2, all of the warp's
+        // rows in flight at once, issued before the barrier that publishes the raw queries),
+        // lanes over the input index; the four heads' sums finish in a transpose-reduce, then a
+        // butterfly over the low three lane bits
         constexpr int RPW = (96 + W - 1) / W;              // rows of R per warp
-        float rr[RPW][3];                                  // all of this warp's rows in flight at once
+        float rr[RPW][3];
         #pragma unroll
         for (int i = 0; i < RPW; ++i) {
             const int k = min(warp + i * W, 95);
             #pragma unroll
             for (int u = 0; u < 3; ++u) rr[i][u] = __ldg(p.R + k * 96 + lane + 32 * u);
         }
+        if (tid < HQ * 96) sQraw[tid] = qreg;
+        named_bar_sync(1, nthr);
         #pragma unroll
         for (int i = 0; i < RPW; ++i) {
             const int k = warp + i * W;
