@@ -109,3 +109,21 @@ def test_grouped_12bit_kernel_streams_balanced_ranges():
     assert p.balanced == 1 and p.smem_bytes <= 227 * 1024 and p.threads == 16 * 32
     p = _plan(_codec(fp32=True), _args(4, 32, 8, 131072, (4, 4, 4), BF16))
     assert p.balanced == 1 and p.smem_bytes <= 227 * 1024 and p.threads == 20 * 32
+
+
+@pytest.mark.parametrize("world", [1, 2, 8])
+def test_exchange_layout_holds_flagged_slots_for_two_calls(world):
+    """The split-sequence exchange buffer: partial slots of 8-byte (value, call flag) words for
+    two call parities and every rank, then the output rows, then the control words."""
+    B, Hq, Hkv, S = 4, 32, 8, 16384
+    lay = _lib.PkvXrLayout()
+    rc = _lib.load().pkv_xr_layout_for(ctypes.byref(_codec()), ctypes.byref(_args(B, Hq, Hkv, S, (4, 4, 4), BF16)),
+                                       world, ctypes.byref(lay))
+    assert rc == 0
+    rows = B * Hq
+    assert lay.rows == rows and lay.units == B * Hq // 4          # grouped 12-bit: four query heads a unit
+    assert lay.out_offset % 256 == 0 and lay.out_offset >= 2 * world * rows * (96 + 2) * 8
+    assert lay.bytes >= lay.out_offset + rows * 96 * 4 + 8
+    bad = _lib.load().pkv_xr_layout_for(ctypes.byref(_codec()), ctypes.byref(_args(B, Hq, Hkv, S, (4, 4, 4), BF16)),
+                                        _lib.XR_MAX_RANKS + 1, ctypes.byref(lay))
+    assert bad != 0
